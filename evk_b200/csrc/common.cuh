@@ -1,0 +1,126 @@
+// common.cuh — shared host/device helpers of libevkcu (status handling,
+// element types, launch accounting, bounded mbarrier waits).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/evkcu.h"
+
+namespace evkcu {
+
+// ---------------------------------------------------------------- status ----
+void set_error(const std::string& msg);
+int fail(int status, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+void count_launch(uint32_t n = 1);
+
+#define EVKCU_CHECK_ARG(cond, status, msg) \
+    do {                                   \
+        if (!(cond)) return ::evkcu::fail((status), (msg)); \
+    } while (0)
+
+#define EVKCU_CUDA_TRY(expr)                                   \
+    do {                                                       \
+        cudaError_t _e = (expr);                               \
+        if (_e != cudaSuccess) return ::evkcu::cuda_fail(_e, #expr); \
+    } while (0)
+
+// Checks the launch that was just enqueued and counts it.
+inline int after_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    count_launch();
+    return EVKCU_OK;
+}
+
+// ------------------------------------------------------ per-device state ----
+// Scratch slots: each op family that needs global scratch owns one, so ops on
+// different streams never share scratch.  Scratch is zero-filled when it is
+// (re)allocated; kernels that use ticket counters leave them at zero.
+enum WorkspaceSlot { WS_GEMV = 0, WS_DECODE = 1, WS_GREEDY = 2, WS_COUNT = 3 };
+
+struct DeviceState {
+    int device = -1;
+    int sm_count = 0;
+    unsigned int* d_error = nullptr;  // device error word for bounded waits
+    void* ws[WS_COUNT] = {};
+    size_t ws_bytes[WS_COUNT] = {};
+};
+// Returns the state of the current device, creating it on first use.
+DeviceState* state();
+// Returns a zero-initialised scratch buffer of at least `bytes` for `slot` on
+// the current device.  Growing it synchronises the device and reallocates, so
+// the first call at a new maximum size must not happen during stream capture.
+void* workspace(int slot, size_t bytes);
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// --------------------------------------------------------- element types ----
+// Storage is 2-byte fp16 (reference) or bf16 (extension); arithmetic is fp32.
+template <typename T> struct Elem;
+template <> struct Elem<__half> {
+    static __device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+    static __device__ __forceinline__ __half from_f(float x) { return __float2half_rn(x); }
+    static __device__ __forceinline__ float2 to_f2(__half2 x) { return __half22float2(x); }
+    static __device__ __forceinline__ __half2 from_f2(float a, float b) { return __floats2half2_rn(a, b); }
+    using T2 = __half2;
+};
+template <> struct Elem<__nv_bfloat16> {
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+    static __device__ __forceinline__ float2 to_f2(__nv_bfloat162 x) { return __bfloat1622float2(x); }
+    static __device__ __forceinline__ __nv_bfloat162 from_f2(float a, float b) { return __floats2bfloat162_rn(a, b); }
+    using T2 = __nv_bfloat162;
+};
+
+// Dispatches a templated launcher on the runtime dtype.
+#define EVKCU_DISPATCH_DTYPE(dtype, T, ...)                                   \
+    [&]() -> int {                                                            \
+        if ((dtype) == EVKCU_F16) { using T = __half; return __VA_ARGS__(); } \
+        if ((dtype) == EVKCU_BF16) { using T = __nv_bfloat16; return __VA_ARGS__(); } \
+        return ::evkcu::fail(EVKCU_BAD_ARG, "unknown dtype");                 \
+    }()
+
+// 16-byte vector of 8 two-byte elements.
+struct __align__(16) Vec8 {
+    uint32_t w[4];
+};
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const Vec8& v, float (&f)[8]) {
+    using T2 = typename Elem<T>::T2;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        T2 h = *reinterpret_cast<const T2*>(&v.w[i]);
+        float2 p = Elem<T>::to_f2(h);
+        f[2 * i] = p.x;
+        f[2 * i + 1] = p.y;
+    }
+}
+template <typename T>
+__device__ __forceinline__ Vec8 pack8(const float (&f)[8]) {
+    using T2 = typename Elem<T>::T2;
+    Vec8 v;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        T2 h = Elem<T>::from_f2(f[2 * i], f[2 * i + 1]);
+        v.w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return v;
+}
+
+// --------------------------------------------------------- device limits ----
+// Upper bound, in clock cycles, of any device-side spin wait (~2 s at 2 GHz).
+// A wait that exceeds it records EVKCU_TIMEOUT in the device error word and
+// gives up instead of hanging the GPU.
+constexpr long long kSpinLimitCycles = 4000000000LL;
+
+}  // namespace evkcu

@@ -1,0 +1,450 @@
+// gemm.cu — evk::ai::matmul on sm_100a.
+//
+// Reference: evk_ai.cpp:254-330 (host), shaders/matmul.comp:44-140 (kernel).
+// The reference runs one 32-lane subgroup per output tile with 16x16x16
+// cooperative-matrix fragments loaded straight from global memory and an fp16
+// accumulator.  Here:
+//
+//  * tcgen05 path (any M): a warp-specialised CTA per 128 x BN output tile.
+//      warp 0 : TMA producer — 128-byte-swizzled A/B k-blocks (64 deep) into
+//               a STAGES-deep shared-memory ring (mbarrier full/empty pairs);
+//      warp 1 : allocates TMEM, one elected lane issues tcgen05.mma
+//               (M=128, N=BN, K=16) into a 128 x BN fp32 TMEM accumulator and
+//               releases each ring slot with tcgen05.commit;
+//      warps 2-5: epilogue — tcgen05.ld of their 32 TMEM lanes, optional
+//               C += (acc_c), one rounding to fp16/bf16, 16-byte stores.
+//    transpose_a / transpose_b select MN-major operand descriptors, so no
+//    operand is ever transposed in memory.  Batch broadcast (stride 0) maps
+//    to a batch extent of 1 in the tensor map.  M/N/K tails are handled by
+//    TMA zero fill and epilogue guards.
+//
+//  * small-M path (decode, M*batch <= 16 with a shared B): a CUDA-core GEMV
+//    that streams B once with 16-byte loads — the weight read is the roofline
+//    there, and a 128-row MMA tile would be 8-128x padded.
+#include <algorithm>
+#include <string>
+
+#include "sm100.cuh"
+
+namespace evkcu {
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kGemmThreads = 192;
+constexpr uint32_t kTimeoutGemm = 0x101;
+
+template <int BN>
+struct GemmCfg {
+    static constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = (196 * 1024) / STAGE_BYTES > 8 ? 8 : (196 * 1024) / STAGE_BYTES;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <typename T, int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, T* __restrict__ C,
+                   uint32_t M, uint32_t N, uint32_t K, uint64_t strideC, int bcastA, int bcastB, int acc_c,
+                   uint32_t idesc, unsigned int* err) {
+    using Cfg = GemmCfg<BN>;
+    constexpr int STAGES = Cfg::STAGES;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + STAGES * Cfg::A_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
+    uint64_t* empty = full + STAGES;
+    uint64_t* accum = empty + STAGES;
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accum + 1);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t n0 = blockIdx.x * BN;
+    const uint32_t m0 = blockIdx.y * BM;
+    const uint32_t bz = blockIdx.z;
+    const int za = bcastA ? 0 : (int)bz;
+    const int zb = bcastB ? 0 : (int)bz;
+    const uint32_t num_kb = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        *s_abort = 0;
+        fence_barrier_init();
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+    }
+    if (warp == 1) {
+        tmem_alloc(s_tmem, BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t ph = (kb / STAGES) & 1;
+                if (!mbar_wait(&empty[s], ph ^ 1, s_abort, err, kTimeoutGemm)) break;
+                mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+                const int k0 = (int)(kb * BK);
+                uint8_t* a = sA + s * Cfg::A_BYTES;
+                uint8_t* b = sB + s * Cfg::B_BYTES;
+                if (!A_MN) {
+                    tma_load_3d(a, &tmA, &full[s], k0, (int)m0, za);
+                } else {
+                    tma_load_3d(a, &tmA, &full[s], (int)m0, k0, za);
+                    tma_load_3d(a + 8192, &tmA, &full[s], (int)m0 + 64, k0, za);
+                }
+                if (!B_MN) {
+                    tma_load_3d(b, &tmB, &full[s], k0, (int)n0, zb);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < BN / 64; ++j) tma_load_3d(b + j * 8192, &tmB, &full[s], (int)n0 + 64 * j, k0, zb);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool ok = true;
+            for (uint32_t kb = 0; kb < num_kb; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t ph = (kb / STAGES) & 1;
+                if (!mbar_wait(&full[s], ph, s_abort, err, kTimeoutGemm)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = smem_u32(sA + s * Cfg::A_BYTES);
+                const uint32_t b = smem_u32(sB + s * Cfg::B_BYTES);
+#pragma unroll
+                for (int k = 0; k < BK / 16; ++k) {
+                    uint64_t ad = A_MN ? make_sw128_desc(a + k * 2048, 8192, 1024) : make_sw128_desc(a + k * 32, 16, 1024);
+                    uint64_t bd = B_MN ? make_sw128_desc(b + k * 2048, 8192, 1024) : make_sw128_desc(b + k * 32, 16, 1024);
+                    mma_f16_ss(tmem, ad, bd, idesc, (kb | k) != 0);
+                }
+                mma_commit(&empty[s]);
+            }
+            if (ok) mma_commit(accum);
+        }
+    } else {
+        // Epilogue warps 2..5 own TMEM lane quarters (warp % 4).
+        const int q = warp & 3;
+        const bool ok = mbar_wait(accum, 0, s_abort, err, kTimeoutGemm);
+        tc_fence_after();
+        if (ok) {
+            const uint32_t row = m0 + q * 32 + lane;
+            T* crow = C + (uint64_t)bz * strideC + (uint64_t)row * N;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, r);
+                tmem_wait_ld();
+                if (row < M) {
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        const uint32_t col = n0 + c * 32 + g * 8;
+                        if (col < N) {
+                            float f[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[g * 8 + e]);
+                            Vec8* dst = reinterpret_cast<Vec8*>(crow + col);
+                            if (acc_c) {
+                                float o[8];
+                                unpack8<T>(*dst, o);
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) f[e] += o[e];
+                            }
+                            *dst = pack8<T>(f);
+                        }
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+}
+
+// --------------------------------------------------------- small-M GEMV ----
+// y[m, n] = sum_k x[m, k] * W[k, n]          (W row-major [K, N], !transpose_b)
+// One CTA = 8 warps over a 256-column slab; warp w takes k = w, w+8, ... of
+// the CTA's K range, each lane 8 consecutive columns (16-byte loads), x rows
+// staged in shared memory.  K is split over gridDim.y CTAs; their fp32
+// partials are combined by the last CTA of each slab (atomic ticket).
+constexpr int kGemvMaxM = 16;
+constexpr int kGemvKChunk = 256;  // k rows staged per shared-memory fill
+
+template <typename T, int MM>
+__global__ void __launch_bounds__(256) gemv_nn_kernel(const T* __restrict__ X, const T* __restrict__ W,
+                                                      T* __restrict__ Y, uint32_t Mt, uint32_t K, uint32_t N,
+                                                      uint32_t k_per_cta, int acc_c, float* __restrict__ partial,
+                                                      unsigned int* __restrict__ tickets) {
+    __shared__ float xs[MM][kGemvKChunk];
+    __shared__ float red[MM][256];  // per-slab sums over the 8 warps (shared atomics)
+    __shared__ bool is_last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t col = blockIdx.x * 256 + lane * 8;
+    const uint32_t kbeg = blockIdx.y * k_per_cta;
+    const uint32_t kend = min(kbeg + k_per_cta, K);
+    float acc[MM][8];
+#pragma unroll
+    for (int m = 0; m < MM; ++m)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[m][e] = 0.0f;
+    for (uint32_t i = threadIdx.x; i < MM * 256; i += blockDim.x) red[i / 256][i % 256] = 0.0f;
+
+    for (uint32_t kc = kbeg; kc < kend; kc += kGemvKChunk) {
+        const uint32_t kn = min((uint32_t)kGemvKChunk, kend - kc);
+        __syncthreads();
+        for (uint32_t i = threadIdx.x; i < MM * kGemvKChunk; i += blockDim.x) {
+            uint32_t m = i / kGemvKChunk, kk = i % kGemvKChunk;
+            xs[m][kk] = (kk < kn && m < Mt) ? Elem<T>::to_f(X[(uint64_t)m * K + kc + kk]) : 0.0f;
+        }
+        __syncthreads();
+        if (col < N) {
+#pragma unroll 4
+            for (uint32_t kk = warp; kk < kn; kk += 8) {
+                float w[8];
+                unpack8<T>(*reinterpret_cast<const Vec8*>(W + (uint64_t)(kc + kk) * N + col), w);
+#pragma unroll
+                for (int m = 0; m < MM; ++m) {
+                    float xv = xs[m][kk];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[m][e] = fmaf(xv, w[e], acc[m][e]);
+                }
+            }
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < MM; ++m)
+        if (m < (int)Mt)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) atomicAdd(&red[m][lane * 8 + e], acc[m][e]);
+    __syncthreads();
+    const uint32_t n_out = Mt * 256;
+    if (gridDim.y == 1) {
+        for (uint32_t i = threadIdx.x; i < n_out; i += blockDim.x) {
+            uint32_t m = i / 256, c = i % 256, n = blockIdx.x * 256 + c;
+            if (n < N) {
+                float v = red[m][c];
+                if (acc_c) v += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
+                Y[(uint64_t)m * N + n] = Elem<T>::from_f(v);
+            }
+        }
+        return;
+    }
+    // Split-K: publish this CTA's partial, the last CTA of the slab reduces.
+    float* my = partial + ((uint64_t)blockIdx.x * gridDim.y + blockIdx.y) * n_out;
+    for (uint32_t i = threadIdx.x; i < n_out; i += blockDim.x) my[i] = red[i / 256][i % 256];
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = atomicAdd(&tickets[blockIdx.x], 1u) == gridDim.y - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const float* base = partial + (uint64_t)blockIdx.x * gridDim.y * n_out;
+    for (uint32_t i = threadIdx.x; i < n_out; i += blockDim.x) {
+        uint32_t m = i / 256, c = i % 256, n = blockIdx.x * 256 + c;
+        float s = 0.0f;
+        for (uint32_t y = 0; y < gridDim.y; ++y) s += ((volatile const float*)base)[(uint64_t)y * n_out + i];
+        if (n < N) {
+            if (acc_c) s += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
+            Y[(uint64_t)m * N + n] = Elem<T>::from_f(s);
+        }
+    }
+    if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
+}
+
+// y[m, n] = sum_k x[m, k] * W[n, k]          (W row-major [N, K], transpose_b)
+// One warp per output column n (all MM rows), lanes split K with 16-byte
+// loads, warp-shuffle reduction.  Used for tied-embedding LM heads.
+template <typename T, int MM>
+__global__ void __launch_bounds__(256) gemv_nt_kernel(const T* __restrict__ X, const T* __restrict__ W,
+                                                      T* __restrict__ Y, uint32_t Mt, uint32_t K, uint32_t N,
+                                                      int acc_c) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t nwarps = gridDim.x * 8;
+    for (uint32_t n = blockIdx.x * 8 + warp; n < N; n += nwarps) {
+        float acc[MM];
+#pragma unroll
+        for (int m = 0; m < MM; ++m) acc[m] = 0.0f;
+        const T* wrow = W + (uint64_t)n * K;
+        for (uint32_t k = lane * 8; k < K; k += 256) {
+            float w[8];
+            unpack8<T>(*reinterpret_cast<const Vec8*>(wrow + k), w);
+#pragma unroll
+            for (int m = 0; m < MM; ++m) {
+                if (m >= (int)Mt) break;
+                float x[8];
+                unpack8<T>(*reinterpret_cast<const Vec8*>(X + (uint64_t)m * K + k), x);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[m] = fmaf(x[e], w[e], acc[m]);
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < MM; ++m) {
+            float v = acc[m];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0 && m < (int)Mt) {
+                if (acc_c) v += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
+                Y[(uint64_t)m * N + n] = Elem<T>::from_f(v);
+            }
+        }
+    }
+}
+
+template <typename T, int BN, bool A_MN, bool B_MN>
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch, uint32_t M, uint32_t N, uint32_t K,
+              uint64_t strideC, int bcastA, int bcastB, int acc, int is_bf16, cudaStream_t st) {
+    using Cfg = GemmCfg<BN>;
+    static bool attr_set = false;
+    auto kern = gemm_tc_kernel<T, BN, A_MN, B_MN>;
+    if (!attr_set) {
+        EVKCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+        attr_set = true;
+    }
+    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
+    uint32_t idesc = make_idesc_f16(BM, BN, is_bf16, A_MN, B_MN);
+    kern<<<grid, kGemmThreads, Cfg::SMEM, st>>>(ta, tb, C, M, N, K, strideC, bcastA, bcastB, acc, idesc,
+                                                state()->d_error);
+    return after_launch("evkcu_matmul(tcgen05)");
+}
+
+template <typename T, int BN>
+int dispatch_major(bool ta, bool tb, const CUtensorMap& mA, const CUtensorMap& mB, T* C, uint32_t batch, uint32_t M,
+                   uint32_t N, uint32_t K, uint64_t sC, int bA, int bB, int acc, int bf, cudaStream_t st) {
+    if (!ta && !tb) return launch_tc<T, BN, false, true>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, st);
+    if (!ta && tb) return launch_tc<T, BN, false, false>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, st);
+    if (ta && !tb) return launch_tc<T, BN, true, true>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, st);
+    return launch_tc<T, BN, true, false>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, st);
+}
+
+template <typename T>
+int launch_gemv(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, bool tb, int acc, cudaStream_t st) {
+    DeviceState* s = state();
+    if (tb) {
+        unsigned grid = (unsigned)std::min<uint64_t>((N + 7) / 8, (uint64_t)s->sm_count * 8);
+        switch ((Mt + 3) / 4) {
+            case 1: gemv_nt_kernel<T, 4><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, acc); break;
+            case 2: gemv_nt_kernel<T, 8><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, acc); break;
+            default: gemv_nt_kernel<T, 16><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, acc); break;
+        }
+        return after_launch("evkcu_matmul(gemv_nt)");
+    }
+    uint32_t slabs = (N + 255) / 256;
+    // Split K so that slabs * splits covers ~2 waves of SMs, 256-row granules.
+    uint32_t want = std::max<uint32_t>(1, (uint32_t)(2 * s->sm_count) / std::max<uint32_t>(1, slabs));
+    uint32_t max_split = std::max<uint32_t>(1, (K + kGemvKChunk - 1) / kGemvKChunk);
+    uint32_t splits = std::min(want, max_split);
+    uint32_t k_per = ((K + splits - 1) / splits + 7) / 8 * 8;
+    splits = (K + k_per - 1) / k_per;
+    float* partial = nullptr;
+    unsigned int* tickets = nullptr;
+    if (splits > 1) {
+        size_t pbytes = (size_t)slabs * splits * Mt * 256 * sizeof(float);
+        size_t tbytes = ((size_t)slabs * 4 + 255) & ~(size_t)255;
+        char* ws = (char*)workspace(WS_GEMV, pbytes + tbytes);
+        if (!ws) return fail(EVKCU_CUDA_ERROR, "evkcu_matmul: workspace allocation failed");
+        tickets = (unsigned int*)ws;
+        partial = (float*)(ws + tbytes);
+    }
+    dim3 grid(slabs, splits);
+    // Tickets start at zero (zero-filled scratch); the reducing CTA resets its entry.
+    switch ((Mt + 3) / 4) {
+        case 1: gemv_nn_kernel<T, 4><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets); break;
+        case 2: gemv_nn_kernel<T, 8><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets); break;
+        default: gemv_nn_kernel<T, 16><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets); break;
+    }
+    return after_launch("evkcu_matmul(gemv_nn)");
+}
+
+}  // namespace
+}  // namespace evkcu
+
+using namespace evkcu;
+
+extern "C" int evkcu_matmul(const void* A, const void* B, void* C, uint32_t batch, uint32_t M, uint32_t K, uint32_t N,
+                            uint64_t stride_a, uint64_t stride_b, uint64_t stride_c, uint32_t flags, int dtype,
+                            void* stream) {
+    if (batch == 0 || M == 0 || N == 0) return EVKCU_OK;
+    EVKCU_CHECK_ARG(A && B && C, EVKCU_BAD_ARG, "evkcu_matmul: null pointer");
+    EVKCU_CHECK_ARG(dtype == EVKCU_F16 || dtype == EVKCU_BF16, EVKCU_BAD_ARG, "evkcu_matmul: unknown dtype");
+    const bool ta = flags & EVKCU_MM_TRANSPOSE_A, tb = flags & EVKCU_MM_TRANSPOSE_B;
+    const int acc = (flags & EVKCU_MM_ACC_C) ? 1 : 0;
+    cudaStream_t st = as_stream(stream);
+    DeviceState* ds = state();
+    EVKCU_CHECK_ARG(ds, EVKCU_CUDA_ERROR, "evkcu_matmul: no device state");
+    EVKCU_CHECK_ARG(N % 8 == 0, EVKCU_BAD_SHAPE, "evkcu_matmul: N must be a multiple of 8");
+    EVKCU_CHECK_ARG(stride_c % 8 == 0 || batch == 1, EVKCU_BAD_ALIGN, "evkcu_matmul: C batch stride must be a multiple of 8");
+    EVKCU_CHECK_ARG(aligned16(A) && aligned16(B) && aligned16(C), EVKCU_BAD_ALIGN,
+                    "evkcu_matmul: base pointers must be 16-byte aligned");
+    if (K == 0) {
+        if (acc) return EVKCU_OK;
+        for (uint32_t b = 0; b < batch; ++b)
+            EVKCU_CUDA_TRY(cudaMemsetAsync((char*)C + (uint64_t)b * stride_c * 2, 0, (uint64_t)M * N * 2, st));
+        return EVKCU_OK;
+    }
+    EVKCU_CHECK_ARG(K % 8 == 0 && (!ta || M % 8 == 0), EVKCU_BAD_SHAPE,
+                    "evkcu_matmul: the contiguous dimension of A and B must be a multiple of 8");
+    const int bf = dtype == EVKCU_BF16 ? 1 : 0;
+
+    // Small-M (decode) path: B shared by the whole batch, A rows contiguous.
+    const bool a_contig = batch == 1 || stride_a == (uint64_t)M * K;
+    const bool c_contig = batch == 1 || stride_c == (uint64_t)M * N;
+    const uint64_t Mt = (uint64_t)batch * M;
+    if (!ta && Mt <= kGemvMaxM && (batch == 1 || stride_b == 0) && a_contig && c_contig) {
+        return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
+            return launch_gemv<T>((const T*)A, (const T*)B, (T*)C, (uint32_t)Mt, K, N, tb, acc, st);
+        });
+    }
+
+    const int bA = (batch > 1 && stride_a == 0) ? 1 : 0;
+    const int bB = (batch > 1 && stride_b == 0) ? 1 : 0;
+    EVKCU_CHECK_ARG(bA || batch == 1 || stride_a % 8 == 0, EVKCU_BAD_ALIGN, "evkcu_matmul: A batch stride % 8");
+    EVKCU_CHECK_ARG(bB || batch == 1 || stride_b % 8 == 0, EVKCU_BAD_ALIGN, "evkcu_matmul: B batch stride % 8");
+
+    // Tile width: the widest BN that still yields >= one wave of CTAs.
+    const uint64_t mt = (M + BM - 1) / BM;
+    auto tiles = [&](uint32_t bn) { return mt * ((N + bn - 1) / bn) * batch; };
+    int BN = 64;
+    if (tiles(256) >= (uint64_t)ds->sm_count) BN = 256;
+    else if (tiles(128) >= (uint64_t)ds->sm_count) BN = 128;
+
+    CUtensorMap mA, mB;
+    const uint32_t zA = bA ? 1 : batch, zB = bB ? 1 : batch;
+    int r;
+    if (!ta)
+        r = make_tmap_3d(&mA, A, K, M, zA, K, (zA > 1 ? stride_a : (uint64_t)M * K), BK, BM, dtype);
+    else
+        r = make_tmap_3d(&mA, A, M, K, zA, M, (zA > 1 ? stride_a : (uint64_t)M * K), 64, BK, dtype);
+    if (r) return r;
+    if (!tb)
+        r = make_tmap_3d(&mB, B, N, K, zB, N, (zB > 1 ? stride_b : (uint64_t)K * N), 64, BK, dtype);
+    else
+        r = make_tmap_3d(&mB, B, K, N, zB, K, (zB > 1 ? stride_b : (uint64_t)K * N), BK, BN, dtype);
+    if (r) return r;
+    const uint64_t sC = batch > 1 ? stride_c : 0;
+    return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
+        if (BN == 256) return dispatch_major<T, 256>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, st);
+        if (BN == 128) return dispatch_major<T, 128>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, st);
+        return dispatch_major<T, 64>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, st);
+    });
+}

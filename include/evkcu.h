@@ -1,0 +1,167 @@
+/*
+ * evkcu.h — C ABI of the B200 (sm_100a) backend for the evk::ai operator set.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA
+ * stream (`void*`, NULL = legacy default stream), enqueues its kernels on that
+ * stream and returns immediately with an evkcu_status.  Nothing here
+ * allocates or frees caller memory.  Tensors use the reference's layout:
+ * row-major, last dimension contiguous, 2-byte elements (fp16, or bf16 as an
+ * extension).  Token ids are raw unsigned integers stored in the element slots
+ * (uint16 as in the reference, or uint32 as an extension for vocabularies
+ * above 65535).
+ *
+ * Each function cites the reference interface it replaces (carloshgsilva/evk,
+ * path:line).  In the reference an op records bind+push+dispatch+barrier into
+ * a global Vulkan command buffer; here stream order replaces the barrier.
+ *
+ * Errors never exit the process: a failing call returns a non-zero status and
+ * evkcu_last_error() returns a message for the calling thread.
+ */
+#ifndef EVKCU_H
+#define EVKCU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum evkcu_status {
+    EVKCU_OK = 0,
+    EVKCU_BAD_SHAPE = 1,   /* shape / size precondition violated               */
+    EVKCU_BAD_ALIGN = 2,   /* pointer or row pitch not aligned as required      */
+    EVKCU_CUDA_ERROR = 3,  /* a CUDA runtime / driver call failed               */
+    EVKCU_COMM_ERROR = 4,  /* a collective failed (tensor-parallel helpers)      */
+    EVKCU_TIMEOUT = 5,     /* a bounded device-side wait gave up                 */
+    EVKCU_UNSUPPORTED = 6, /* valid request this build does not implement        */
+    EVKCU_BAD_ARG = 7      /* null pointer / invalid enum                        */
+} evkcu_status;
+
+typedef enum evkcu_dtype {
+    EVKCU_F16 = 0,  /* the reference's only storage type (evk_ai.h:252-260) */
+    EVKCU_BF16 = 1  /* extension for the bf16 LLM configurations            */
+} evkcu_dtype;
+
+/* matmul flags, evk_ai.h:495 (transpose_a, transpose_b, acc_c) */
+#define EVKCU_MM_TRANSPOSE_A 1u
+#define EVKCU_MM_TRANSPOSE_B 2u
+#define EVKCU_MM_ACC_C 4u
+
+/* flash attention flags (extension: the reference is non-causal only) */
+#define EVKCU_ATTN_CAUSAL 1u
+
+/* ---- context -------------------------------------------------------------
+ * Replaces evk::ai::initialize / shutdown (evk_ai.h:489-490, evk_ai.cpp:211-252):
+ * selects the device and creates the per-device state (SM count, device error
+ * word, small workspace).  Every op calls it lazily for the current device.   */
+int evkcu_init(int device);
+int evkcu_shutdown(void);
+const char* evkcu_last_error(void);
+const char* evkcu_version(void);
+/* Reads and clears the device error word written by bounded device-side waits
+ * (EVKCU_TIMEOUT when a kernel gave up waiting).  Synchronises the device.   */
+int evkcu_check_device_error(void);
+/* Number of kernels this library launched on the calling thread since the
+ * last reset (evidence for the benchmark's gpu_launches field).              */
+uint64_t evkcu_launch_count(void);
+void evkcu_reset_launch_count(void);
+
+/* ---- matmul ----------------------------------------------------------------
+ * evk::ai::matmul  evk_ai.h:495, evk_ai.cpp:254-330, shaders/matmul.comp:44-140
+ * C[b] = op(A[b]) . op(B[b])  (+ C[b] when EVKCU_MM_ACC_C)
+ *   op(A) is M x K: A is stored [M,K] row-major, or [K,M] with TRANSPOSE_A.
+ *   op(B) is K x N: B is stored [K,N] row-major, or [N,K] with TRANSPOSE_B.
+ *   C is [M,N] row-major.  stride_a/b/c are per-batch element strides; 0 means
+ *   the operand is broadcast over the batch (evk_ai.cpp:299-304).
+ * fp32 accumulation on tcgen05 tensor cores, one rounding to the storage type.
+ * Requires the contiguous dimension of each operand to be a multiple of 8
+ * elements and 16-byte aligned base pointers.  Unlike the reference, M, N and K
+ * need not be tile multiples: tails are computed, not left unwritten.        */
+int evkcu_matmul(const void* A, const void* B, void* C,
+                 uint32_t batch, uint32_t M, uint32_t K, uint32_t N,
+                 uint64_t stride_a, uint64_t stride_b, uint64_t stride_c,
+                 uint32_t flags, int dtype, void* stream);
+
+/* ---- flash attention -------------------------------------------------------
+ * evk::ai::flash_attention  evk_ai.h:497-501, evk_ai.cpp:332-369,
+ * shaders/flash_attention.comp:53-185.
+ * O = softmax(Q_h K_g^T * scale) V_g per batch b, query head h, with KV head
+ * g = h / (H / Hkv).  Q, O: [B, N, H*Dh];  K, V: [B, N, Hkv*Dh].
+ * The reference call is Hkv = 1 (multi-query), non-causal, scale = 1/sqrt(Dh);
+ * Hkv = H (per-head K/V) and EVKCU_ATTN_CAUSAL are extensions.
+ * Rows whose softmax denominator is 0 produce 0 (flash_attention.comp:166).
+ * Dh must be a multiple of 16 and at most 256.                              */
+int evkcu_flash_attention(const void* q, const void* k, const void* v, void* o,
+                          uint32_t B, uint32_t N, uint32_t H, uint32_t Hkv, uint32_t Dh,
+                          float scale, uint32_t flags, int dtype, void* stream);
+
+/* ---- single-query (decode) attention --------------------------------------
+ * shaders/single_query_attention.comp:27-71 (the reference ships the shader
+ * without a host wrapper; this is that wrapper, generalised to B sequences,
+ * H query heads over Hkv cached heads, and any cache length).
+ * q, out: [B, H*Dh];  kcache, vcache: [B, max_len, Hkv*Dh];  attends over the
+ * first cur_len positions of each sequence.  scale <= 0 selects 1/sqrt(Dh)
+ * (the shader's inversesqrt(dim)).                                           */
+int evkcu_single_query_attention(const void* q, const void* kcache, const void* vcache, void* out,
+                                 uint32_t B, uint32_t H, uint32_t Hkv, uint32_t Dh,
+                                 uint32_t max_len, uint32_t cur_len, float scale,
+                                 int dtype, void* stream);
+
+/* ---- row / elementwise ops ------------------------------------------------ */
+
+/* evk::ai::rms_norm  evk_ai.h:607-610, evk_ai.cpp:1045-1067, shaders/rms_norm.comp:21-48
+ * y = clamp(x, +-65504) * rsqrt(mean(clamp(x)^2) + eps) per row of D.
+ * gamma (optional, [D], extension) multiplies the result when non-NULL.      */
+int evkcu_rms_norm(const void* in, void* out, const void* gamma,
+                   uint32_t rows, uint32_t D, float eps, int dtype, void* stream);
+
+/* evk::ai::rope  evk_ai.h:587-591, evk_ai.cpp:945-966, shaders/rope.comp:18-40
+ * Interleaved pairs (x[2i], x[2i+1]) rotated by angle t*base^(-2i/rot_dim).
+ * in/out: [batch, seq_len, dim].  The reference is head_dim = dim and
+ * pos_offset = 0; head_dim < dim rotates each head_dim slice independently and
+ * pos_offset shifts t (decode), both extensions.                             */
+int evkcu_rope(const void* in, void* out, uint32_t batch, uint32_t seq_len, uint32_t dim,
+               uint32_t head_dim, uint32_t pos_offset, float base, int dtype, void* stream);
+
+/* evk::ai::gelu  evk_ai.h:538-540, evk_ai.cpp:679-699, shaders/gelu.comp:15-29 (tanh form) */
+int evkcu_gelu(const void* in, void* out, uint64_t n, int dtype, void* stream);
+
+/* evk::ai::softmax  evk_ai.h:523-525, evk_ai.cpp:593-613, shaders/softmax.comp:23-66
+ * Row softmax of raw*scale over L; raw <= -65504 is masked (output 0).       */
+int evkcu_softmax(const void* in, void* out, uint32_t rows, uint32_t L, float scale,
+                  int dtype, void* stream);
+
+/* evk::ai::add  evk_ai.h:520-521, evk_ai.cpp:568-591, shaders/add.comp:18-26 */
+int evkcu_add(const void* a, const void* b, void* c, uint64_t n, int dtype, void* stream);
+
+/* evk::ai::scale  evk_ai.cpp:992-1007, shaders/scale.comp (in place)        */
+int evkcu_scale(void* x, uint64_t n, float s, int dtype, void* stream);
+
+/* evk::ai::zero  evk_ai.cpp:1010-1024, shaders/zero.comp                    */
+int evkcu_zero(void* x, uint64_t n, int dtype, void* stream);
+
+/* evk::ai::apply_causal_mask  evk_ai.h:574-577, evk_ai.cpp:862-882,
+ * shaders/causal_mask.comp:16-33: scores[b,i,j] = -65504 for j > i.          */
+int evkcu_causal_mask(void* scores, uint32_t batch, uint32_t N, int dtype, void* stream);
+
+/* evk::ai::embed  evk_ai.h:554-558, evk_ai.cpp:782-806, shaders/embed.comp:18-28
+ * out[i,:] = E[idx[i],:].  idx_bytes = 2 (reference uint16) or 4 (extension).
+ * Indices >= vocab are clamped to vocab-1 instead of reading out of bounds.  */
+int evkcu_embed(const void* E, const void* idx, void* out, uint32_t vocab, uint32_t dim,
+                uint32_t n_idx, uint32_t idx_bytes, int dtype, void* stream);
+
+/* evk::ai::greedy_sample  evk_ai.h:560-566, evk_ai.cpp:808-837,
+ * shaders/greedy_sample.comp:24-64.
+ * out[b] = argmax_j logits[b, position, token_base + j], j < token_count, with
+ * the reference's exact tie rule (256-lane strided scan keeping the first
+ * strict maximum, then a strict-greater tree: ties go to the lower lane).
+ * out_bytes = 2 (uint16, reference) or 4 (uint32 extension).                 */
+int evkcu_greedy_sample(const void* logits, void* out, uint32_t B, uint32_t S, uint32_t V,
+                        uint32_t position, uint32_t token_base, uint32_t token_count,
+                        uint32_t out_bytes, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* EVKCU_H */
