@@ -1,0 +1,344 @@
+"""Benchmark: evk::ai flash-attention forward on B200.
+
+One step = one evk::ai flash-attention forward over one batch of the C2
+configuration (B=4, H=16, S=2048, Dh=64, causal, fp16 Q/K/V ~ N(0,1), seeded,
+per-head K/V), launched through the C ABI (evkcu_flash_attention).
+
+  value  device throughput, inputs resident in HBM: algorithmic FLOPs
+         (4*B*H*S^2*Dh / 2 for causal) / CUDA-event time of K steps.  Steps
+         rotate over input sets totalling > 3x the 126 MB L2, so no step
+         reads a predecessor's inputs from L2.
+  e2e    the same metric through the same C ABI call with HOST buffers:
+         per step, pinned-host Q/K/V -> device, the kernel, O -> host.
+  roofline  tensor-bound; achieved TFLOP/s of the flash kernel (measured with
+         CUDA events on its launch stream) over the measured bf16 dense peak.
+  cpu_baseline  the CPU oracle (C++ restatement of the reference's shader
+         math) on a bounded sample of (batch, head) pairs of the same workload.
+
+With --impl reference the CPU implementation (the reference's Vulkan path
+cannot run here) is timed on the host cores on the same
+workload and metric.  Multi-GPU (torchrun): each rank runs its own C2 batch
+(weak scaling, no collective); value = total FLOPs / max over ranks.
+Extra keys report the GEMM leg (8192^3 bf16 matmul TFLOP/s) for context.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B, H, S, DH = 4, 16, 2048, 64
+CAUSAL = True
+FLOPS = 4.0 * B * H * S * S * DH / (2.0 if CAUSAL else 1.0)
+METRIC = "flash-attn fwd TFLOP/s (C2: B4 H16 S2048 Dh64 causal)"
+CONFIG = {
+    "workload": "evk::ai flash_attention fwd, C2 B=4 H=16 S=2048 Dh=64 causal, per-head K/V",
+    "global_batch": B,
+    "seq_len": S,
+    "heads": H,
+    "head_dim": DH,
+    "causal": CAUSAL,
+    "l2": "inputs rotate over sets totalling > 3x L2",
+}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["bf16_tflops"], p["hbm_gbs"], "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = "clocks.sm,clocks.max.sm,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown," \
+             "clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 7:
+                self.samples.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = sorted(float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit())
+        mx = max((float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[3 + i].lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def cpu_baseline(budget_s: float = 10.0, threads: int | None = None):
+    """Times the CPU oracle on whole (batch, head) slices of the C2 workload."""
+    import numpy as np
+
+    import oracle
+
+    if threads:
+        os.environ["EVK_ORACLE_THREADS"] = str(threads)
+    n = S * DH
+    q, k, v = (oracle.normal(n, s) for s in (11, 12, 13))
+    o = np.empty_like(q)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        oracle.flash_attention(q, k, v, o, 1, S, 1, 1, DH, 0.0, 1 if CAUSAL else 0, 0)
+        done += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    flops = done * 4.0 * S * S * DH / (2.0 if CAUSAL else 1.0)
+    return {
+        "value": flops / dt / 1e12,
+        "unit": "TFLOP/s",
+        "cores": oracle.num_threads(),
+        "sample": f"{done} of the {B * H} (batch, head) slices of C2 (S=2048, Dh=64, causal), {dt:.1f} s",
+    }
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    # The reference runs its kernels as Vulkan compute shaders; neither Vulkan
+    # nor a software renderer exists on these machines, so the reference arm
+    # is the reference's algorithm restated on the CPU (the oracle), timed on
+    # all host threads over a bounded sample per step.
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline(budget_s=0.5)
+    for _ in range(args.steps):
+        vals.append(cpu_baseline(budget_s=2.0)["value"])
+    cb = cpu_baseline(budget_s=2.0)
+    value = sorted(vals)[len(vals) // 2]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": FLOPS / (value * 1e12) * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": CONFIG,
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cb["cores"], "kind": "port",
+                         "sample": "per step: " + cb["sample"]},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "CPU oracle (restatement of the reference shaders); the reference's Vulkan path is unavailable on this box",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def gemm_leg(torch, evk, dtype, n=8192, reps=20):
+    a = torch.randn(n, n, device="cuda").to(dtype)
+    b = torch.randn(n, n, device="cuda").to(dtype)
+    c = torch.empty(n, n, device="cuda", dtype=dtype)
+    for _ in range(3):
+        evk.matmul(a, b, c)
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(reps):
+        evk.matmul(a, b, c)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / reps
+    return 2.0 * n ** 3 / (ms * 1e-3) / 1e12
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="evk_b200", choices=["evk_b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+
+    import evk_b200 as evk
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    evk.init(local)
+    dtype = torch.float16
+    stream = torch.cuda.current_stream()
+
+    # Input sets: enough that the rotation never hits L2 (3x 126 MB).
+    set_bytes = 4 * B * S * H * DH * 2
+    nsets = max(2, int((3 * 126e6) // set_bytes) + 1)
+    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    sets = []
+    for _ in range(nsets):
+        q, k, v = (torch.randn(B, S, H * DH, device="cuda", generator=g).to(dtype) for _ in range(3))
+        sets.append((q, k, v, torch.empty_like(q)))
+
+    def step(i):
+        q, k, v, o = sets[i % nsets]
+        evk.flash_attention(q, k, v, o, heads=H, causal=CAUSAL, stream=stream)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    # ------------------------------------------------ device-timed region --
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        evk.reset_launch_count()
+        start.record(stream)
+        for i in range(args.steps):
+            step(i)
+        end.record(stream)
+        torch.cuda.synchronize()
+        launches = evk.launch_count()
+        if ws > 1:
+            torch.distributed.barrier()
+    ms_total = start.elapsed_time(end)
+    if ws > 1:
+        t = torch.tensor([ms_total], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_total = t.item()
+    ms_step = ms_total / args.steps
+    value = FLOPS * ws / (ms_step * 1e-3) / 1e12
+    kernel_tflops = FLOPS / (ms_step * 1e-3) / 1e12
+    evk.check_device_error()
+
+    # ------------------------------------------------------ end-to-end leg --
+    hq, hk, hv = (t.cpu().pin_memory() for t in sets[0][:3])
+    ho = torch.empty_like(hq).pin_memory()
+    dq, dk, dv, do = (torch.empty_like(sets[0][0]) for _ in range(4))
+    e2e_steps = max(3, min(50, args.steps // 20))
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        evk.flash_attention(dq, dk, dv, do, heads=H, causal=CAUSAL, stream=stream)
+        ho.copy_(do, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if ws > 1:
+        torch.distributed.barrier()
+    es.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ee.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = es.elapsed_time(ee) / e2e_steps
+    if ws > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = t.item()
+    e2e_val = FLOPS * ws / (e2e_ms * 1e-3) / 1e12
+    # Parity spot-check of the copied result against the resident run.
+    evk.flash_attention(*sets[0], heads=H, causal=CAUSAL, stream=stream)
+    torch.cuda.synchronize()
+    assert torch.equal(ho.cuda(), sets[0][3]), "e2e output differs from the device-resident run"
+
+    extra = {}
+    if not args.no_extra:
+        extra["gemm_8192_bf16_tflops"] = round(gemm_leg(torch, evk, torch.bfloat16), 1)
+        extra["gemm_8192_f16_tflops"] = round(gemm_leg(torch, evk, torch.float16), 1)
+
+    if ws > 1:
+        torch.distributed.barrier()
+    if rank != 0:
+        torch.distributed.destroy_process_group()
+        return
+
+    tf_peak, _, peak_kind = peaks()
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        try:
+            traffic = json.load(open(tpath)).get("flash_tc_kernel_c2_bytes_per_launch")
+        except Exception:
+            traffic = None
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic",
+        "config": dict(CONFIG, parallelism=f"replicas x{ws} (independent C2 batches)"),
+        "e2e": {"value": round(e2e_val, 2), "unit": "TFLOP/s", "h2d_bytes_per_step": 3 * hq.numel() * 2,
+                "d2h_bytes_per_step": ho.numel() * 2},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "achieved": round(kernel_tflops, 2), "peak": tf_peak, "unit": "TFLOP/s",
+                     "frac": round(kernel_tflops / tf_peak, 4), "peak_kind": f"bf16 dense burst, {peak_kind}",
+                     "traffic": traffic},
+        "clocks": clocks.summary(),
+        "extra": extra,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = dict(cpu_baseline(budget_s=10.0), kind="port")
+    print(json.dumps(line), flush=True)
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,282 @@
+"""evk_b200 — B200 (sm_100a) backend for the evk::ai inference operators.
+
+The product is the C ABI in ``include/evkcu.h`` (``libevkcu.so``) and the
+C++20 ``evk::ai`` layer above it (``libevk_ai.so``).  This module binds the C
+ABI with ctypes so Python callers (tests, ``bench.py``) can drive the kernels
+on torch-allocated device memory.  It is a thin binding: no kernel runs
+anywhere but in ``libevkcu.so``, and importing it fails loudly when the
+library has not been built.
+
+Function names follow the reference's operators (carloshgsilva/evk
+``evk_ai.h:489-615``); argument meaning follows ``include/evkcu.h``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libevkcu.so")
+AI_LIB_PATH = os.path.join(_HERE, "libevk_ai.so")
+
+F16 = 0
+BF16 = 1
+MM_TRANSPOSE_A = 1
+MM_TRANSPOSE_B = 2
+MM_ACC_C = 4
+ATTN_CAUSAL = 1
+
+STATUS = {
+    0: "OK",
+    1: "BAD_SHAPE",
+    2: "BAD_ALIGN",
+    3: "CUDA_ERROR",
+    4: "COMM_ERROR",
+    5: "TIMEOUT",
+    6: "UNSUPPORTED",
+    7: "BAD_ARG",
+}
+
+
+class EvkcuError(RuntimeError):
+    def __init__(self, op: str, status: int, msg: str):
+        super().__init__(f"{op} failed: {STATUS.get(status, status)}: {msg}")
+        self.status = status
+
+
+_u32, _u64, _f32, _int, _vp = ctypes.c_uint32, ctypes.c_uint64, ctypes.c_float, ctypes.c_int, ctypes.c_void_p
+
+# name -> argtypes (all return int status unless listed in _RET)
+SIGNATURES = {
+    "evkcu_init": [_int],
+    "evkcu_shutdown": [],
+    "evkcu_last_error": [],
+    "evkcu_version": [],
+    "evkcu_check_device_error": [],
+    "evkcu_launch_count": [],
+    "evkcu_reset_launch_count": [],
+    "evkcu_matmul": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u64, _u64, _u64, _u32, _int, _vp],
+    "evkcu_flash_attention": [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _u32, _int, _vp],
+    "evkcu_single_query_attention": [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _f32, _int, _vp],
+    "evkcu_rms_norm": [_vp, _vp, _vp, _u32, _u32, _f32, _int, _vp],
+    "evkcu_rope": [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _int, _vp],
+    "evkcu_gelu": [_vp, _vp, _u64, _int, _vp],
+    "evkcu_softmax": [_vp, _vp, _u32, _u32, _f32, _int, _vp],
+    "evkcu_add": [_vp, _vp, _vp, _u64, _int, _vp],
+    "evkcu_scale": [_vp, _u64, _f32, _int, _vp],
+    "evkcu_zero": [_vp, _u64, _int, _vp],
+    "evkcu_causal_mask": [_vp, _u32, _u32, _int, _vp],
+    "evkcu_embed": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _int, _vp],
+    "evkcu_greedy_sample": [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _int, _vp],
+}
+_RET = {
+    "evkcu_last_error": ctypes.c_char_p,
+    "evkcu_version": ctypes.c_char_p,
+    "evkcu_launch_count": ctypes.c_uint64,
+    "evkcu_reset_launch_count": None,
+}
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Loads libevkcu.so and declares every C-ABI entry point."""
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is missing: build it with `make -C evk_b200` (or __graft_entry__.build())")
+    lib = ctypes.CDLL(path)
+    for name, args in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = _RET.get(name, ctypes.c_int)
+    return lib
+
+
+_lib: Optional[ctypes.CDLL] = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        _lib = load_library()
+    return _lib
+
+
+def _check(op: str, status: int) -> None:
+    if status != 0:
+        raise EvkcuError(op, status, lib().evkcu_last_error().decode())
+
+
+def _dtype_code(t) -> int:
+    import torch
+
+    if t.dtype == torch.float16:
+        return F16
+    if t.dtype == torch.bfloat16:
+        return BF16
+    raise TypeError(f"unsupported dtype {t.dtype}: evk tensors are 2-byte fp16 (or bf16)")
+
+
+def _ptr(t) -> int:
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("evk_b200 ops take CUDA tensors")
+    if not t.is_contiguous():
+        raise ValueError("evk_b200 ops take contiguous (row-major) tensors")
+    return t.data_ptr()
+
+
+def _stream(stream) -> int:
+    import torch
+
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    return getattr(stream, "cuda_stream", stream)
+
+
+def init(device: int = -1) -> None:
+    _check("evkcu_init", lib().evkcu_init(device))
+
+
+def launch_count() -> int:
+    return int(lib().evkcu_launch_count())
+
+
+def reset_launch_count() -> None:
+    lib().evkcu_reset_launch_count()
+
+
+def check_device_error() -> None:
+    _check("evkcu_check_device_error", lib().evkcu_check_device_error())
+
+
+# ------------------------------------------------------------------ operators
+def matmul(a, b, c, transpose_a=False, transpose_b=False, acc_c=False, stream=None):
+    """evk::ai::matmul (evk_ai.cpp:254-330): c = op(a) @ op(b) (+ c).
+
+    Shapes follow the reference: (..., M, K) x (..., K, N) -> (..., M, N); an
+    operand whose leading dims multiply to 1 is broadcast over the batch.
+    """
+    def lead(t):
+        n = 1
+        for d in t.shape[:-2]:
+            n *= d
+        return n
+
+    ba, bb, bc = lead(a), lead(b), lead(c)
+    batch = max(ba, bb, bc)
+    M = a.shape[-1] if transpose_a else a.shape[-2]
+    K = a.shape[-2] if transpose_a else a.shape[-1]
+    N = b.shape[-2] if transpose_b else b.shape[-1]
+    Kb = b.shape[-1] if transpose_b else b.shape[-2]
+    if Kb != K or c.shape[-2] != M or c.shape[-1] != N or bc != batch or ba not in (1, batch) or bb not in (1, batch):
+        raise EvkcuError("matmul", 1, f"incompatible shapes {tuple(a.shape)} {tuple(b.shape)} {tuple(c.shape)}")
+    ea, eb, ec = a.shape[-2] * a.shape[-1], b.shape[-2] * b.shape[-1], c.shape[-2] * c.shape[-1]
+    sa = 0 if (ba == 1 and batch > 1) else ea
+    sb = 0 if (bb == 1 and batch > 1) else eb
+    flags = (MM_TRANSPOSE_A if transpose_a else 0) | (MM_TRANSPOSE_B if transpose_b else 0) | (MM_ACC_C if acc_c else 0)
+    _check("evkcu_matmul", lib().evkcu_matmul(_ptr(a), _ptr(b), _ptr(c), batch, M, K, N, sa, sb, ec, flags,
+                                              _dtype_code(a), _stream(stream)))
+    return c
+
+
+def flash_attention(q, k, v, o, heads: Optional[int] = None, causal=False, scale: float = 0.0, stream=None):
+    """evk::ai::flash_attention (evk_ai.cpp:332-369) plus extensions.
+
+    q, o: (B, N, H*Dh); k, v: (B, N, Hkv*Dh).  Without `heads` the reference's
+    multi-query call is assumed (Hkv = 1, Dh = k.shape[-1]).  `heads` gives H
+    (Dh = q.shape[-1] // H, Hkv = k.shape[-1] // Dh).
+    """
+    B, N, D = q.shape
+    if heads is None:
+        Dh = k.shape[-1]
+        H, Hkv = D // Dh, 1
+    else:
+        H = heads
+        Dh = D // H
+        Hkv = k.shape[-1] // Dh
+    _check("evkcu_flash_attention", lib().evkcu_flash_attention(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(o), B, N, H, Hkv, Dh, scale, ATTN_CAUSAL if causal else 0,
+        _dtype_code(q), _stream(stream)))
+    return o
+
+
+def single_query_attention(q, kcache, vcache, out, heads: int, cur_len: int, scale: float = 0.0, stream=None):
+    """Decode attention over a KV cache (shaders/single_query_attention.comp).
+
+    q, out: (B, H*Dh); kcache, vcache: (B, max_len, Hkv*Dh).
+    """
+    B = q.shape[0]
+    Dh = q.shape[-1] // heads
+    max_len = kcache.shape[1]
+    Hkv = kcache.shape[-1] // Dh
+    _check("evkcu_single_query_attention", lib().evkcu_single_query_attention(
+        _ptr(q), _ptr(kcache), _ptr(vcache), _ptr(out), B, heads, Hkv, Dh, max_len, cur_len, scale,
+        _dtype_code(q), _stream(stream)))
+    return out
+
+
+def rms_norm(x, out, eps=1e-4, gamma=None, stream=None):
+    D = x.shape[-1]
+    _check("evkcu_rms_norm", lib().evkcu_rms_norm(_ptr(x), _ptr(out), _ptr(gamma), x.numel() // D, D, eps,
+                                                  _dtype_code(x), _stream(stream)))
+    return out
+
+
+def rope(x, out, batch, seq_len, dim, base=10000.0, head_dim=0, pos_offset=0, stream=None):
+    _check("evkcu_rope", lib().evkcu_rope(_ptr(x), _ptr(out), batch, seq_len, dim, head_dim, pos_offset, base,
+                                          _dtype_code(x), _stream(stream)))
+    return out
+
+
+def gelu(x, out, stream=None):
+    _check("evkcu_gelu", lib().evkcu_gelu(_ptr(x), _ptr(out), x.numel(), _dtype_code(x), _stream(stream)))
+    return out
+
+
+def softmax(x, out, scale=1.0, stream=None):
+    L = x.shape[-1]
+    _check("evkcu_softmax", lib().evkcu_softmax(_ptr(x), _ptr(out), x.numel() // L, L, scale, _dtype_code(x),
+                                                _stream(stream)))
+    return out
+
+
+def add(a, b, c, stream=None):
+    _check("evkcu_add", lib().evkcu_add(_ptr(a), _ptr(b), _ptr(c), a.numel(), _dtype_code(a), _stream(stream)))
+    return c
+
+
+def scale(x, s, stream=None):
+    _check("evkcu_scale", lib().evkcu_scale(_ptr(x), x.numel(), s, _dtype_code(x), _stream(stream)))
+    return x
+
+
+def zero(x, stream=None):
+    _check("evkcu_zero", lib().evkcu_zero(_ptr(x), x.numel(), _dtype_code(x), _stream(stream)))
+    return x
+
+
+def apply_causal_mask(s, stream=None):
+    N = s.shape[-1]
+    _check("evkcu_causal_mask", lib().evkcu_causal_mask(_ptr(s), s.numel() // (N * N), N, _dtype_code(s),
+                                                        _stream(stream)))
+    return s
+
+
+def embed(E, idx, out, stream=None):
+    """idx: int16/uint16 (reference) or int32 ids, any shape."""
+    import torch
+
+    ib = 2 if idx.element_size() == 2 else 4
+    _check("evkcu_embed", lib().evkcu_embed(_ptr(E), _ptr(idx), _ptr(out), E.shape[0], E.shape[1], idx.numel(), ib,
+                                            _dtype_code(E), _stream(stream)))
+    return out
+
+
+def greedy_sample(logits, out, position, token_base, token_count, stream=None):
+    """logits (B, S, V); out (B,) int16/uint16 (reference) or int32 ids."""
+    B, S, V = logits.shape
+    ob = 2 if out.element_size() == 2 else 4
+    _check("evkcu_greedy_sample", lib().evkcu_greedy_sample(
+        _ptr(logits), _ptr(out), B, S, V, position, token_base, token_count, ob, _dtype_code(logits),
+        _stream(stream)))
+    return out

@@ -56,6 +56,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     while (true) {
         if (mbar_try_wait(a, parity)) return true;
         if (*abort) return false;
+        // Another CTA already gave up: stop waiting on work that may never come.
+        if (err && *reinterpret_cast<volatile unsigned int*>(err)) {
+            *abort = 1;
+            return false;
+        }
         if (clock64() - t0 > kSpinLimitCycles) {
             *abort = 1;
             if (err) atomicCAS(err, 0u, code);
