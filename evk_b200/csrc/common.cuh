@@ -59,6 +59,13 @@ DeviceState* state();
 // the first call at a new maximum size must not happen during stream capture.
 void* workspace(int slot, size_t bytes);
 
+// Every scratch slot starts with a fixed ticket area (split reductions'
+// atomic counters, left at zero by the kernels) followed by the partials, so
+// calls with different grid shapes never see each other's partials as
+// tickets.
+constexpr size_t kTicketBytes = 256 * 1024;
+constexpr uint32_t kMaxTickets = kTicketBytes / sizeof(unsigned int);
+
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

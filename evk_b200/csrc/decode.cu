@@ -208,7 +208,8 @@ int launch_decode(const void* q, const void* k, const void* v, void* o, uint32_t
     chunk = (chunk + 31) / 32 * 32;
     const uint32_t nsplit = (cur_len + chunk - 1) / chunk;
     const size_t pbytes = (size_t)B * H * nsplit * (Dh + 2) * sizeof(float);
-    const size_t toff = ((size_t)ctas_wo_split * 4 + 255) & ~(size_t)255;
+    if (ctas_wo_split > kMaxTickets) return fail(EVKCU_BAD_SHAPE, "evkcu_single_query_attention: B*Hkv too large");
+    const size_t toff = kTicketBytes;
     char* ws = (char*)workspace(WS_DECODE, toff + pbytes);
     if (!ws) return fail(EVKCU_CUDA_ERROR, "evkcu_single_query_attention: scratch allocation failed");
     dim3 grid(nsplit, Hkv * hgroups, B);

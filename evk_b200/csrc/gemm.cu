@@ -360,7 +360,8 @@ int launch_gemv(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t 
     unsigned int* tickets = nullptr;
     if (splits > 1) {
         size_t pbytes = (size_t)slabs * splits * Mt * 256 * sizeof(float);
-        size_t tbytes = ((size_t)slabs * 4 + 255) & ~(size_t)255;
+        if (slabs > kMaxTickets) return fail(EVKCU_BAD_SHAPE, "evkcu_matmul: N too large for the GEMV path");
+        const size_t tbytes = kTicketBytes;
         char* ws = (char*)workspace(WS_GEMV, pbytes + tbytes);
         if (!ws) return fail(EVKCU_CUDA_ERROR, "evkcu_matmul: workspace allocation failed");
         tickets = (unsigned int*)ws;

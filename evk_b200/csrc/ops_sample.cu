@@ -149,7 +149,8 @@ extern "C" int evkcu_greedy_sample(const void* logits, void* out, uint32_t B, ui
     unsigned int* tickets = nullptr;
     uint64_t* partial = nullptr;
     if (chunks > 1) {
-        size_t toff = ((size_t)B * 4 + 255) & ~(size_t)255;
+        EVKCU_CHECK_ARG(B <= kMaxTickets, EVKCU_BAD_SHAPE, "evkcu_greedy_sample: batch too large");
+        const size_t toff = kTicketBytes;
         char* ws = (char*)workspace(WS_GREEDY, toff + (size_t)B * chunks * 8);
         EVKCU_CHECK_ARG(ws, EVKCU_CUDA_ERROR, "evkcu_greedy_sample: scratch allocation failed");
         tickets = (unsigned int*)ws;

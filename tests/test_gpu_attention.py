@@ -150,3 +150,18 @@ def test_single_query_attention_empty_cache_is_zero():
     kc = torch.randn(1, 16, 128, device="cuda").half()
     ev().single_query_attention(q, kc, kc, out, 2, 0)
     assert bool((out == 0).all())
+
+
+def test_single_query_attention_scratch_reuse_across_shapes():
+    """Split-reduction scratch is shared by calls of different grid shapes:
+    a large call after a small one must not read stale counters."""
+    for (B, H, Dh, L, cur) in [(8, 16, 128, 256, 64), (1, 2, 128, 256, 200), (8, 16, 64, 256, 64), (8, 16, 128, 256, 64)]:
+        q = oracle.normal(B * H * Dh, 51)
+        kc = oracle.normal(B * L * H * Dh, 52)
+        vc = oracle.normal(B * L * H * Dh, 53)
+        out = torch.empty(B, H * Dh, dtype=torch.float16, device="cuda")
+        ev().single_query_attention(dev(q, torch.float16).view(B, H * Dh), dev(kc, torch.float16).view(B, L, H * Dh),
+                                    dev(vc, torch.float16).view(B, L, H * Dh), out, H, cur)
+        r = np.empty(B * H * Dh, np.uint16)
+        oracle.single_query_attention(q, kc, vc, r, B, H, H, Dh, L, cur)
+        assert_close(u16(out).ravel(), r, 0, what=f"decode reuse {(B, H, Dh, L, cur)}")

@@ -98,11 +98,13 @@ def test_matmul_large_vs_torch_fp32(dtype, M, K, N):
     b = torch.randn(K, N, device="cuda", generator=g).to(dtype)
     c = torch.empty(M, N, dtype=dtype, device="cuda")
     ev().matmul(a, b, c)
-    ref = (a.float() @ b.float())
+    # fp32 reference rounded once to the storage type (as the oracle does):
+    # what remains is accumulation order, at most ~1 storage ulp per element.
+    ref = (a.float() @ b.float()).to(dtype).float()
     err = (c.float() - ref)
     rel = err.norm() / ref.norm()
     tol_elem = (2e-2 + (2 ** -10 if dtype == torch.float16 else 2 ** -7) * ref.abs())
-    assert rel.item() <= 1e-3, f"rel-L2 {rel.item()}"
+    assert rel.item() <= (1e-3 if dtype == torch.float16 else 2e-3), f"rel-L2 {rel.item()}"
     assert bool((err.abs() <= tol_elem).all()), f"max abs err {err.abs().max().item()}"
 
 
