@@ -8,19 +8,12 @@
 // with a zero denominator produce 0, Q/O laid out [B, N, H*Dh] and K/V
 // [B, N, Hkv*Dh] (the reference call is Hkv = 1, non-causal).
 //
-// tcgen05 kernel (Dh = 64 or 128), one CTA per (128-query tile, head, batch):
-//   warp 0   TMA producer: Q once, then K_j / V_j 128-key blocks into a
-//            STAGES-deep ring (separate K and V barriers).
-//   warp 1   TMEM owner + MMA issuer:  S_j = Q K_j^T  (M=128,N=128,K=Dh) into
-//            one of two TMEM S buffers, then PV_{j-1} = P_{j-1} V_{j-1}
-//            (M=128, N=Dh, K=128) into one of two TMEM PV buffers, so the
-//            tensor core computes S_{j+1} while the softmax warps work on S_j.
-//   warps 2-5 softmax, one thread per query row (its TMEM lane): row max and
-//            exp2 over S_j, P_j -> shared memory (fp16/bf16, 128-byte swizzled
-//            K-major, the A operand of the PV MMA), then O = O*alpha + PV in
-//            fp32 registers; final 1/l and 16-byte stores.
-// Causal tiles stop at the diagonal block; only diagonal / ragged blocks
-// evaluate the mask.
+// tcgen05 kernel (Dh = 64 or 128): one CTA per NT consecutive 128-query
+// tiles of one (batch, head); see flash_tc_kernel for the warp roles.  S and
+// O live in TMEM; P goes through shared memory as the A operand of the PV
+// MMA; O is rescaled lazily (FlashAttention-4 style) only when a row's
+// running max grows by more than 2^8.  Causal tiles stop at the diagonal
+// block; only diagonal / ragged blocks evaluate the mask.
 //
 // Any other Dh (multiple of 16, <= 256) runs a CUDA-core kernel (one warp per
 // query row) with the same semantics.
@@ -35,27 +28,31 @@ namespace {
 
 using namespace sm100;
 
-constexpr int FM = 128;  // queries per CTA
+constexpr int FM = 128;  // queries per tile (one TMEM lane per query)
 constexpr int FN = 128;  // keys per block
-constexpr int kFlashThreads = 192;
 constexpr uint32_t kTimeoutFlash = 0x201;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
-template <int DH>
+// NT query tiles per CTA, each with its own softmax warpgroup, share every
+// K/V block.  Dh = 64 runs NT = 2 (two warpgroups ping-pong on the tensor
+// core); Dh = 128 runs NT = 1 to fit shared memory.
+template <int DH, int NT>
 struct FlashCfg {
-    static constexpr int Q_BYTES = FM * DH * 2;
-    static constexpr int K_BYTES = FN * DH * 2;
-    static constexpr int V_BYTES = FN * DH * 2;
-    static constexpr int P_BYTES = FM * FN * 2;  // one P buffer
-    static constexpr int STAGES = DH == 64 ? 3 : 2;
+    static constexpr int Q_BYTES = FM * DH * 2;  // per tile
+    static constexpr int KV_BYTES = FN * DH * 2;  // one K or V block
+    static constexpr int P_BYTES = FM * FN * 2;  // per tile
+    static constexpr int STAGES = NT == 2 ? 3 : (DH == 64 ? 4 : 2);
     static constexpr int OFF_Q = 0;
-    static constexpr int OFF_P = OFF_Q + Q_BYTES;
-    static constexpr int OFF_K = OFF_P + 2 * P_BYTES;
-    static constexpr int OFF_V = OFF_K + STAGES * K_BYTES;
-    static constexpr int OFF_BAR = OFF_V + STAGES * V_BYTES;
+    static constexpr int OFF_P = OFF_Q + NT * Q_BYTES;
+    static constexpr int OFF_K = OFF_P + NT * P_BYTES;
+    static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
+    static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;
-    static constexpr uint32_t TMEM_COLS = 512;
-    static constexpr uint32_t COL_S = 0;        // two S buffers: 0, 128
-    static constexpr uint32_t COL_PV = 2 * FN;  // two PV buffers: 256, 256 + DH
+    static constexpr int THREADS = 128 + NT * 128;
+    static constexpr uint32_t TMEM_COLS = NT == 2 ? 512 : 256;
+    // tile t: S (fp32, 128 cols) at t*256, O (fp32, DH cols) at t*256 + 128
+    static __device__ __forceinline__ uint32_t col_s(int t) { return t * 256; }
+    static __device__ __forceinline__ uint32_t col_o(int t) { return t * 256 + 128; }
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -66,14 +63,27 @@ __device__ __forceinline__ float ex2(float x) {
 
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-template <typename T, int DH>
-__global__ void __launch_bounds__(kFlashThreads, 1)
+// One CTA = NT consecutive 128-query tiles of one (batch, head).
+//   warp 0       TMA producer: Q tiles once, then K_j / V_j blocks into a
+//                STAGES-deep ring (separate K and V barriers).
+//   warp 1       TMEM owner + MMA issuer.  For each block j: S_t(j) = Q_t K_j^T
+//                for every tile (S_t(j) may start as soon as softmax t has
+//                read S_t(j-1) into registers), then O_t += P_t(j-1) V_{j-1}
+//                accumulated in TMEM.
+//   warps 2-3    idle.
+//   warpgroup 1+t  softmax of tile t, one thread per query row (= TMEM lane):
+//                one TMEM load of the S row, row max, lazy rescale of the O row
+//                in TMEM (only when the running max grows by > 2^8), P = exp2
+//                into shared memory (128-byte-swizzled K-major, the A operand
+//                of the PV MMA), finally O / l from TMEM to global memory.
+template <typename T, int DH, int NT>
+__global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
     flash_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, T* __restrict__ O, uint32_t N, uint32_t H,
                     uint32_t Hkv, float scale_log2, int causal, uint32_t idesc_s, uint32_t idesc_pv,
                     unsigned int* err) {
-    using Cfg = FlashCfg<DH>;
-    constexpr int STAGES = Cfg::STAGES;
+    using Cfg = FlashCfg<DH, NT>;
+    constexpr int ST = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem + Cfg::OFF_Q;
@@ -81,16 +91,15 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
     uint8_t* sK = smem + Cfg::OFF_K;
     uint8_t* sV = smem + Cfg::OFF_V;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
-    uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;               // [STAGES]
-    uint64_t* v_full = k_full + STAGES;        // [STAGES]
-    uint64_t* kv_empty = v_full + STAGES;      // [STAGES]
-    uint64_t* s_full = kv_empty + STAGES;      // [2]
-    uint64_t* s_free = s_full + 2;             // [2]
-    uint64_t* p_full = s_free + 2;             // [2]
-    uint64_t* pv_full = p_full + 2;            // [2]
-    uint64_t* pv_free = pv_full + 2;           // [2]
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(pv_free + 2);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = q_full + 1;      // [ST]
+    uint64_t* v_full = k_full + ST;     // [ST]
+    uint64_t* kv_empty = v_full + ST;   // [ST]
+    uint64_t* s_full = kv_empty + ST;   // [NT]
+    uint64_t* s_free = s_full + NT;     // [NT]
+    uint64_t* p_full = s_free + NT;     // [NT]
+    uint64_t* pv_done = p_full + NT;    // [NT]
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(pv_done + NT);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -98,25 +107,28 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
     const uint32_t bh = blockIdx.x;
     const uint32_t b = bh / H, h = bh % H;
     const uint32_t g = h / (H / Hkv);
-    const uint32_t num_qt = gridDim.y;
-    const uint32_t qt = num_qt - 1 - blockIdx.y;  // heaviest causal tiles first
-    const uint32_t q0 = qt * FM;
-    const uint32_t kv_blocks_all = (N + FN - 1) / FN;
-    const uint32_t nblk = causal ? min(kv_blocks_all, (q0 + FM + FN - 1) / FN) : kv_blocks_all;
+    const uint32_t grp = gridDim.y - 1 - blockIdx.y;  // heaviest causal tiles first
+    const uint32_t kv_all = (N + FN - 1) / FN;
+    uint32_t q0[NT], nblk[NT], nmax = 0;
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        q0[t] = (grp * NT + t) * FM;
+        nblk[t] = q0[t] < N ? (causal ? min(kv_all, q0[t] / FN + 1) : kv_all) : 0;
+        nmax = max(nmax, nblk[t]);
+    }
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < ST; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&v_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 4);
-            mbar_init(&p_full[i], 4);
-            mbar_init(&pv_full[i], 1);
-            mbar_init(&pv_free[i], 4);
+        for (int t = 0; t < NT; ++t) {
+            mbar_init(&s_full[t], 1);
+            mbar_init(&s_free[t], 4);
+            mbar_init(&p_full[t], 4);
+            mbar_init(&pv_done[t], 1);
         }
         *s_abort = 0;
         fence_barrier_init();
@@ -136,23 +148,25 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------ TMA producer ----
         if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, Cfg::Q_BYTES);
+            mbar_arrive_expect_tx(q_full, NT * Cfg::Q_BYTES);
 #pragma unroll
-            for (int c = 0; c < DH / 64; ++c)
-                tma_load_3d(sQ + c * FM * 128, &tmQ, q_full, (int)(h * DH + c * 64), (int)q0, (int)b);
-            for (uint32_t j = 0; j < nblk; ++j) {
-                const int st = j % STAGES;
-                const uint32_t ph = (j / STAGES) & 1;
-                if (!mbar_wait(&kv_empty[st], ph ^ 1, s_abort, err, kTimeoutFlash)) break;
-                mbar_arrive_expect_tx(&k_full[st], Cfg::K_BYTES);
+            for (int t = 0; t < NT; ++t)
 #pragma unroll
                 for (int c = 0; c < DH / 64; ++c)
-                    tma_load_3d(sK + st * Cfg::K_BYTES + c * FN * 128, &tmK, &k_full[st], (int)(g * DH + c * 64),
+                    tma_load_3d(sQ + t * Cfg::Q_BYTES + c * FM * 128, &tmQ, q_full, (int)(h * DH + c * 64), (int)q0[t],
+                                (int)b);
+            for (uint32_t j = 0; j < nmax; ++j) {
+                const int st = j % ST;
+                if (!mbar_wait(&kv_empty[st], ((j / ST) & 1) ^ 1, s_abort, err, kTimeoutFlash)) break;
+                mbar_arrive_expect_tx(&k_full[st], Cfg::KV_BYTES);
+#pragma unroll
+                for (int c = 0; c < DH / 64; ++c)
+                    tma_load_3d(sK + st * Cfg::KV_BYTES + c * FN * 128, &tmK, &k_full[st], (int)(g * DH + c * 64),
                                 (int)(j * FN), (int)b);
-                mbar_arrive_expect_tx(&v_full[st], Cfg::V_BYTES);
+                mbar_arrive_expect_tx(&v_full[st], Cfg::KV_BYTES);
 #pragma unroll
                 for (int c = 0; c < DH / 64; ++c)
-                    tma_load_3d(sV + st * Cfg::V_BYTES + c * FN * 128, &tmV, &v_full[st], (int)(g * DH + c * 64),
+                    tma_load_3d(sV + st * Cfg::KV_BYTES + c * FN * 128, &tmV, &v_full[st], (int)(g * DH + c * 64),
                                 (int)(j * FN), (int)b);
             }
         }
@@ -162,178 +176,175 @@ __global__ void __launch_bounds__(kFlashThreads, 1)
             bool ok = mbar_wait(q_full, 0, s_abort, err, kTimeoutFlash);
             tc_fence_after();
             const uint32_t qaddr = smem_u32(sQ);
+            const uint32_t paddr = smem_u32(sP);
             auto issue_pv = [&](uint32_t jj) -> bool {
-                const int st = jj % STAGES;
-                const int pb = jj & 1;
-                if (!mbar_wait(&p_full[pb], (jj >> 1) & 1, s_abort, err, kTimeoutFlash)) return false;
-                if (!mbar_wait(&pv_free[pb], ((jj >> 1) & 1) ^ 1, s_abort, err, kTimeoutFlash)) return false;
-                if (!mbar_wait(&v_full[st], (jj / STAGES) & 1, s_abort, err, kTimeoutFlash)) return false;
-                tc_fence_after();
-                const uint32_t paddr = smem_u32(sP + pb * Cfg::P_BYTES);
-                const uint32_t vaddr = smem_u32(sV + st * Cfg::V_BYTES);
+                const int st = jj % ST;
+                if (!mbar_wait(&v_full[st], (jj / ST) & 1, s_abort, err, kTimeoutFlash)) return false;
+                const uint32_t vaddr = smem_u32(sV + st * Cfg::KV_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < FN / 16; ++kk) {
-                    uint64_t ad = make_sw128_desc(paddr + (kk >> 2) * (FM * 128) + (kk & 3) * 32, 16, 1024);
-                    uint64_t bd = make_sw128_desc(vaddr + kk * 2048, FN * 128, 1024);
-                    mma_f16_ss(tmem + Cfg::COL_PV + pb * DH, ad, bd, idesc_pv, kk != 0);
+                for (int t = 0; t < NT; ++t) {
+                    if (jj >= nblk[t]) continue;
+                    if (!mbar_wait(&p_full[t], jj & 1, s_abort, err, kTimeoutFlash)) return false;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < FN / 16; ++kk) {
+                        uint64_t ad = make_sw128_desc(paddr + t * Cfg::P_BYTES + (kk >> 2) * (FM * 128) + (kk & 3) * 32,
+                                                      16, 1024);
+                        uint64_t bd = make_sw128_desc(vaddr + kk * 2048, FN * 128, 1024);
+                        mma_f16_ss(tmem + Cfg::col_o(t), ad, bd, idesc_pv, (jj | kk) != 0);
+                    }
+                    mma_commit(&pv_done[t]);
                 }
-                mma_commit(&pv_full[pb]);
                 mma_commit(&kv_empty[st]);
                 return true;
             };
-            for (uint32_t j = 0; ok && j < nblk; ++j) {
-                const int st = j % STAGES;
-                const int sb = j & 1;
-                if (!mbar_wait(&k_full[st], (j / STAGES) & 1, s_abort, err, kTimeoutFlash)) break;
-                if (!mbar_wait(&s_free[sb], ((j >> 1) & 1) ^ 1, s_abort, err, kTimeoutFlash)) break;
-                tc_fence_after();
-                const uint32_t kaddr = smem_u32(sK + st * Cfg::K_BYTES);
+            for (uint32_t j = 0; ok && j < nmax; ++j) {
+                const int st = j % ST;
+                if (!mbar_wait(&k_full[st], (j / ST) & 1, s_abort, err, kTimeoutFlash)) break;
+                const uint32_t kaddr = smem_u32(sK + st * Cfg::KV_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < DH / 16; ++kk) {
-                    uint64_t ad = make_sw128_desc(qaddr + (kk >> 2) * (FM * 128) + (kk & 3) * 32, 16, 1024);
-                    uint64_t bd = make_sw128_desc(kaddr + (kk >> 2) * (FN * 128) + (kk & 3) * 32, 16, 1024);
-                    mma_f16_ss(tmem + Cfg::COL_S + sb * FN, ad, bd, idesc_s, kk != 0);
+                for (int t = 0; t < NT; ++t) {
+                    if (j >= nblk[t]) continue;
+                    if (j >= 1 && !mbar_wait(&s_free[t], (j - 1) & 1, s_abort, err, kTimeoutFlash)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < DH / 16; ++kk) {
+                        uint64_t ad = make_sw128_desc(qaddr + t * Cfg::Q_BYTES + (kk >> 2) * (FM * 128) + (kk & 3) * 32,
+                                                      16, 1024);
+                        uint64_t bd = make_sw128_desc(kaddr + (kk >> 2) * (FN * 128) + (kk & 3) * 32, 16, 1024);
+                        mma_f16_ss(tmem + Cfg::col_s(t), ad, bd, idesc_s, kk != 0);
+                    }
+                    mma_commit(&s_full[t]);
                 }
-                mma_commit(&s_full[sb]);
-                if (j >= 1 && !issue_pv(j - 1)) {
-                    ok = false;
-                    break;
-                }
+                if (ok && j >= 1 && !issue_pv(j - 1)) ok = false;
             }
-            if (ok && nblk > 0) issue_pv(nblk - 1);
+            if (ok && nmax > 0) issue_pv(nmax - 1);
         }
-    } else {
+    } else if (warp >= 4) {
         // --------------------------------------------- softmax warps ----
+        const int t = (warp >> 2) - 1;
         const int quarter = warp & 3;
-        const uint32_t row = quarter * 32 + lane;  // TMEM lane == query row in tile
-        const uint32_t qidx = q0 + row;
+        const uint32_t row = quarter * 32 + lane;  // TMEM lane == query row in the tile
+        const uint32_t qidx = q0[t] + row;
         const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-        float o[DH];
-#pragma unroll
-        for (int d = 0; d < DH; ++d) o[d] = 0.0f;
-        float m = -INFINITY, l = 0.0f;
+        const uint32_t s_addr = lane_addr + Cfg::col_s(t);
+        const uint32_t o_addr = lane_addr + Cfg::col_o(t);
+        const uint32_t kmax = min(N, causal ? qidx + 1 : N);  // keys < kmax are valid
+        uint8_t* prow = sP + t * Cfg::P_BYTES + row * 128;
+        float m_ref = -INFINITY, l = 0.0f;
         bool ok = true;
-        for (uint32_t j = 0; j < nblk; ++j) {
-            const int sb = j & 1;
-            if (!mbar_wait(&s_full[sb], (j >> 1) & 1, s_abort, err, kTimeoutFlash)) {
+        const uint32_t nb = nblk[t];
+        for (uint32_t j = 0; j < nb; ++j) {
+            if (!mbar_wait(&s_full[t], j & 1, s_abort, err, kTimeoutFlash)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t k0 = j * FN;
-            const bool need_mask = (k0 + FN > N) || (causal && k0 + FN > q0 + 1);
-            // A key is valid when it exists and (non-causal or key <= query).
-            const uint32_t kmax = min(N, causal ? qidx + 1 : N);  // keys < kmax are valid
-            const uint32_t s_addr = lane_addr + Cfg::COL_S + sb * FN;
-            // pass 1: row max of the scaled scores
-            float mx = -INFINITY;
+            uint32_t sr[FN / 32][32];
 #pragma unroll
-            for (int c = 0; c < FN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(s_addr + c * 32, r);
-                tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    float v = __uint_as_float(r[e]);
-                    if (need_mask && k0 + c * 32 + e >= kmax) v = -INFINITY;
-                    mx = fmaxf(mx, v);
-                }
-            }
-            const float m_new = fmaxf(m, mx * scale_log2);
-            const float m_use = (m_new == -INFINITY) ? 0.0f : m_new;
-            const float alpha = ex2(m - m_use);  // m = -inf -> 0
-            // pass 2: p = exp2(s*scale_log2 - m), row sum, P -> shared memory
-            float rs = 0.0f;
-            uint8_t* prow = sP + sb * Cfg::P_BYTES + row * 128;
-#pragma unroll
-            for (int c = 0; c < FN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld32(s_addr + c * 32, r);
-                tmem_wait_ld();
-                float p[32];
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    float v = __uint_as_float(r[e]);
-                    float pe = ex2(fmaf(v, scale_log2, -m_use));
-                    if (need_mask && k0 + c * 32 + e >= kmax) pe = 0.0f;
-                    p[e] = pe;
-                    rs += pe;
-                }
-                // 32 keys = 4 16-byte chunks; key block (c*32)/64, chunk index within the 128-byte row.
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int key = c * 32 + q * 8;
-                    const int blk = key >> 6;
-                    const int chunk = (key & 63) >> 3;
-                    float f[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) f[e] = p[q * 8 + e];
-                    Vec8 v8 = pack8<T>(f);
-                    *reinterpret_cast<Vec8*>(prow + blk * (FM * 128) + ((chunk ^ (row & 7)) << 4)) = v8;
-                }
-            }
-            // S buffer consumed: release it to the MMA warp.
+            for (int c = 0; c < FN / 32; ++c) tmem_ld32(s_addr + c * 32, sr[c]);
+            tmem_wait_ld();
+            // S is in registers: the tensor core may overwrite it with S_t(j+1).
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[sb]);
-            // P written by generic stores: make it visible to the tensor core.
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[sb]);
-            l = l * alpha + rs;
-            m = m_new;
-            // Fold in PV_{j-1} (relative to the previous max), then rescale.
-            if (j >= 1) {
-                const uint32_t jj = j - 1;
-                const int pb = jj & 1;
-                if (!mbar_wait(&pv_full[pb], (jj >> 1) & 1, s_abort, err, kTimeoutFlash)) {
+            if (lane == 0) mbar_arrive(&s_free[t]);
+
+            const uint32_t k0 = j * FN;
+            const bool need_mask = (k0 + FN > N) || (causal && j + 1 == nb);
+            float mx = -INFINITY;
+            if (need_mask) {
+#pragma unroll
+                for (int c = 0; c < FN / 32; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        if (k0 + c * 32 + e >= kmax) sr[c][e] = __float_as_uint(-INFINITY);
+                        mx = fmaxf(mx, __uint_as_float(sr[c][e]));
+                    }
+            } else {
+#pragma unroll
+                for (int c = 0; c < FN / 32; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[c][e]));
+            }
+            const float m_cand = fmaxf(m_ref, mx * scale_log2);
+            // Lazy rescale: keep the reference max unless it grew by > 2^8.
+            const bool need = j > 0 && m_cand > m_ref + kRescaleThreshold;
+            const float alpha = need ? ex2(m_ref - m_cand) : 1.0f;  // m_ref = -inf -> 0
+            if (j == 0 || need) m_ref = m_cand;
+            if (j > 0) {
+                // PV_t(j-1) must be complete before the P buffer is reused
+                // and before O is rescaled.
+                if (!mbar_wait(&pv_done[t], (j - 1) & 1, s_abort, err, kTimeoutFlash)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+            }
+            const float m_use = (m_ref == -INFINITY) ? 0.0f : m_ref;
+            float rs = 0.0f;
+#pragma unroll
+            for (int c = 0; c < FN / 32; ++c) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        // masked entries hold -inf: exp2(-inf) = 0
+                        f[e] = ex2(fmaf(__uint_as_float(sr[c][q * 8 + e]), scale_log2, -m_use));
+                        rs += f[e];
+                    }
+                    const int key = c * 32 + q * 8;
+                    const int chunk = (key & 63) >> 3;
+                    *reinterpret_cast<Vec8*>(prow + (key >> 6) * (FM * 128) + ((chunk ^ (row & 7)) << 4)) =
+                        pack8<T>(f);
+                }
+            }
+            l = l * alpha + rs;
+            if (__any_sync(0xffffffffu, need)) {
 #pragma unroll
                 for (int c = 0; c < DH / 32; ++c) {
                     uint32_t r[32];
-                    tmem_ld32(lane_addr + Cfg::COL_PV + pb * DH + c * 32, r);
+                    tmem_ld32(o_addr + c * 32, r);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) o[c * 32 + e] = (o[c * 32 + e] + __uint_as_float(r[e])) * alpha;
+                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+                    tmem_st32(o_addr + c * 32, r);
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&pv_free[pb]);
-            } else {
-#pragma unroll
-                for (int d = 0; d < DH; ++d) o[d] *= alpha;
+                tmem_wait_st();
             }
+            // P (generic-proxy stores) and any O rescale must be visible to the
+            // tensor core before the PV MMA is issued.
+            fence_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[t]);
         }
-        if (ok && nblk > 0) {
-            const uint32_t jj = nblk - 1;
-            const int pb = jj & 1;
-            ok = mbar_wait(&pv_full[pb], (jj >> 1) & 1, s_abort, err, kTimeoutFlash);
+        if (ok && nb > 0) {
+            ok = mbar_wait(&pv_done[t], (nb - 1) & 1, s_abort, err, kTimeoutFlash);
             tc_fence_after();
             if (ok) {
+                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+                T* orow = O + ((uint64_t)b * N + qidx) * ((uint64_t)H * DH) + (uint64_t)h * DH;
 #pragma unroll
                 for (int c = 0; c < DH / 32; ++c) {
                     uint32_t r[32];
-                    tmem_ld32(lane_addr + Cfg::COL_PV + pb * DH + c * 32, r);
+                    tmem_ld32(o_addr + c * 32, r);
                     tmem_wait_ld();
+                    if (qidx < N) {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) o[c * 32 + e] += __uint_as_float(r[e]);
+                        for (int q = 0; q < 4; ++q) {
+                            float f[8];
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[q * 8 + e]) * inv;
+                            reinterpret_cast<Vec8*>(orow + c * 32)[q] = pack8<T>(f);
+                        }
+                    }
                 }
             }
             tc_fence_before();
-        }
-        if (ok && qidx < N) {
-            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            T* orow = O + ((uint64_t)b * N + qidx) * ((uint64_t)H * DH) + (uint64_t)h * DH;
-#pragma unroll
-            for (int c = 0; c < DH / 8; ++c) {
-                float f[8];
-#pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = o[c * 8 + e] * inv;
-                reinterpret_cast<Vec8*>(orow)[c] = pack8<T>(f);
-            }
         }
     }
     __syncthreads();
@@ -398,16 +409,16 @@ __global__ void __launch_bounds__(256) flash_simt_kernel(const T* __restrict__ Q
     }
 }
 
-template <typename T, int DH>
+template <typename T, int DH, int NT>
 int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N, uint32_t H,
                     uint32_t Hkv, float scale_log2, int causal, int dtype, cudaStream_t st) {
-    using Cfg = FlashCfg<DH>;
+    using Cfg = FlashCfg<DH, NT>;
     CUtensorMap mQ, mK, mV;
     int r;
     if ((r = make_tmap_3d(&mQ, q, (uint64_t)H * DH, N, B, (uint64_t)H * DH, (uint64_t)N * H * DH, 64, FM, dtype))) return r;
     if ((r = make_tmap_3d(&mK, k, (uint64_t)Hkv * DH, N, B, (uint64_t)Hkv * DH, (uint64_t)N * Hkv * DH, 64, FN, dtype))) return r;
     if ((r = make_tmap_3d(&mV, v, (uint64_t)Hkv * DH, N, B, (uint64_t)Hkv * DH, (uint64_t)N * Hkv * DH, 64, FN, dtype))) return r;
-    auto kern = flash_tc_kernel<T, DH>;
+    auto kern = flash_tc_kernel<T, DH, NT>;
     static bool attr = false;
     if (!attr) {
         EVKCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
@@ -416,9 +427,10 @@ int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32
     const int bf = dtype == EVKCU_BF16 ? 1 : 0;
     const uint32_t idesc_s = make_idesc_f16(FM, FN, bf, 0, 0);
     const uint32_t idesc_pv = make_idesc_f16(FM, DH, bf, 0, 1);
-    dim3 grid(B * H, (N + FM - 1) / FM);
-    kern<<<grid, kFlashThreads, Cfg::SMEM, st>>>(mQ, mK, mV, (T*)o, N, H, Hkv, scale_log2, causal, idesc_s, idesc_pv,
-                                                 state()->d_error);
+    const uint32_t qtiles = (N + FM - 1) / FM;
+    dim3 grid(B * H, (qtiles + NT - 1) / NT);
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(mQ, mK, mV, (T*)o, N, H, Hkv, scale_log2, causal, idesc_s, idesc_pv,
+                                                state()->d_error);
     return after_launch("evkcu_flash_attention(tcgen05)");
 }
 
@@ -445,8 +457,8 @@ extern "C" int evkcu_flash_attention(const void* q, const void* k, const void* v
     const bool tma_ok = aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
     if (tma_ok && (Dh == 64 || Dh == 128)) {
         return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-            if (Dh == 64) return launch_flash_tc<T, 64>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, st);
-            return launch_flash_tc<T, 128>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, st);
+            if (Dh == 64) return launch_flash_tc<T, 64, 2>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, st);
+            return launch_flash_tc<T, 128, 1>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, st);
         });
     }
     const uint64_t warps = (uint64_t)B * H * N;
