@@ -69,6 +69,7 @@ SIGNATURES = {
     "evkcu_causal_mask": [_vp, _u32, _u32, _int, _vp],
     "evkcu_embed": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _int, _vp],
     "evkcu_greedy_sample": [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _int, _vp],
+    "evkcu_greedy_sample_noalloc": [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _int, _vp],
 }
 _RET = {
     "evkcu_last_error": ctypes.c_char_p,

@@ -18,6 +18,8 @@
 // ticket) reduces them and writes the id, so one launch does the whole op.
 #include <float.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace evkcu {
@@ -161,5 +163,76 @@ extern "C" int evkcu_greedy_sample(const void* logits, void* out, uint32_t B, ui
         greedy_kernel<T><<<grid, kThreads, 0, as_stream(stream)>>>((const T*)logits, out, S, V, position, token_base,
                                                                   token_count, out_bytes, partial, tickets);
         return after_launch("evkcu_greedy_sample");
+    });
+}
+
+// ---------------------------------------------------------------------------
+// evkcu_greedy_sample_noalloc — the same kernel with its split-reduction
+// scratch in a fixed, file-scope device array instead of library-allocated
+// memory, for callers that must not allocate (see evkcu.h).
+namespace evkcu {
+namespace {
+
+// [kNoAllocTickets] ticket counters, then the per-chunk partial keys.
+constexpr size_t kNoAllocScratchBytes = 128 * 1024;
+constexpr uint32_t kNoAllocTickets = 1024;
+constexpr size_t kNoAllocKeyOffset = kNoAllocTickets * sizeof(unsigned int);
+constexpr size_t kNoAllocMaxKeys = (kNoAllocScratchBytes - kNoAllocKeyOffset) / sizeof(uint64_t);
+
+static __device__ __align__(256) unsigned char g_greedy_noalloc_scratch[kNoAllocScratchBytes];
+
+// Device address of the array, looked up once per device with that device
+// current.  Host code cannot use the symbol itself: on the host it names a
+// stand-in object, not the device memory.
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    EVKCU_CUDA_TRY(cudaGetDevice(&dev));
+    EVKCU_CHECK_ARG(dev >= 0 && dev < 64, EVKCU_UNSUPPORTED, "evkcu_greedy_sample_noalloc: device index >= 64");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        EVKCU_CUDA_TRY(cudaGetSymbolAddress(&p, g_greedy_noalloc_scratch));
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return EVKCU_OK;
+}
+
+}  // namespace
+}  // namespace evkcu
+
+extern "C" int evkcu_greedy_sample_noalloc(const void* logits, void* out, uint32_t B, uint32_t S, uint32_t V,
+                                           uint32_t position, uint32_t token_base, uint32_t token_count,
+                                           uint32_t out_bytes, int dtype, void* stream) {
+    if (B == 0) return EVKCU_OK;
+    EVKCU_CHECK_ARG(logits && out, EVKCU_BAD_ARG, "evkcu_greedy_sample_noalloc: null pointer");
+    EVKCU_CHECK_ARG(out_bytes == 2 || out_bytes == 4, EVKCU_BAD_ARG,
+                    "evkcu_greedy_sample_noalloc: out_bytes must be 2 or 4");
+    EVKCU_CHECK_ARG(position < S, EVKCU_BAD_SHAPE, "evkcu_greedy_sample_noalloc: position >= seq_len");
+    EVKCU_CHECK_ARG((uint64_t)token_base + token_count <= V, EVKCU_BAD_SHAPE,
+                    "evkcu_greedy_sample_noalloc: token window exceeds vocabulary");
+    const uint32_t chunks = token_count == 0 ? 1 : (token_count + kChunk - 1) / kChunk;
+    EVKCU_CHECK_ARG(B <= kNoAllocTickets && (uint64_t)B * chunks <= kNoAllocMaxKeys, EVKCU_BAD_SHAPE,
+                    "evkcu_greedy_sample_noalloc: request exceeds the fixed scratch (needs B <= 1024 and "
+                    "B * ceil(token_count / 4096) <= 15872); use evkcu_greedy_sample");
+    unsigned int* tickets = nullptr;
+    uint64_t* partial = nullptr;
+    if (chunks > 1) {
+        void* base = nullptr;
+        const int r = noalloc_scratch(&base);
+        if (r != EVKCU_OK) return r;
+        tickets = static_cast<unsigned int*>(base);
+        partial = reinterpret_cast<uint64_t*>(static_cast<char*>(base) + kNoAllocKeyOffset);
+        // The array keeps the previous call's contents: the tickets must start at zero.
+        EVKCU_CUDA_TRY(cudaMemsetAsync(tickets, 0, (size_t)B * sizeof(unsigned int), as_stream(stream)));
+    }
+    dim3 grid(chunks, B);
+    return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
+        greedy_kernel<T><<<grid, kThreads, 0, as_stream(stream)>>>((const T*)logits, out, S, V, position, token_base,
+                                                                  token_count, out_bytes, partial, tickets);
+        return after_launch("evkcu_greedy_sample_noalloc");
     });
 }

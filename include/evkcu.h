@@ -161,6 +161,25 @@ int evkcu_greedy_sample(const void* logits, void* out, uint32_t B, uint32_t S, u
                         uint32_t position, uint32_t token_base, uint32_t token_count,
                         uint32_t out_bytes, int dtype, void* stream);
 
+/* No counterpart in the reference.  Same arguments, result and tie rule as
+ * evkcu_greedy_sample, for callers that cannot allocate GPU memory when they
+ * call it: code that runs while a CUDA stream is being captured (cudaMalloc
+ * is not allowed there), serving loops that reserve all HBM up front for
+ * weights and KV cache, and host programs that forbid allocation on their hot
+ * path.  This entry point never allocates or frees memory: its scratch is one
+ * fixed 128 KiB device array inside the library, which every GPU that loads
+ * the library keeps until the process exits.
+ *   - Limit: B <= 1024 and B * ceil(token_count / 4096) <= 15872; larger
+ *     requests return EVKCU_BAD_SHAPE (use evkcu_greedy_sample for those).
+ *   - The first call on a device looks up the array's device address with
+ *     that device current; make that first call before any stream capture.
+ *   - All calls on a device share that device's array, which keeps the last
+ *     call's contents: calls that overlap on the GPU (for example on two
+ *     streams of one device) race and must be ordered by the caller.        */
+int evkcu_greedy_sample_noalloc(const void* logits, void* out, uint32_t B, uint32_t S, uint32_t V,
+                                uint32_t position, uint32_t token_base, uint32_t token_count,
+                                uint32_t out_bytes, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
