@@ -187,6 +187,27 @@ def gemm_leg(torch, evk, dtype, n=8192, reps=20):
     return 2.0 * n ** 3 / (ms * 1e-3) / 1e12
 
 
+def profile_leg(leg):
+    """A few launches of one leg on resident inputs: the small case ncu captures."""
+    import torch
+
+    import evk_b200 as evk
+
+    evk.init(0)
+    if leg == "flash":
+        q, k, v = (torch.randn(B, S, H * DH, device="cuda").half() for _ in range(3))
+        o = torch.empty_like(q)
+        for _ in range(5):
+            evk.flash_attention(q, k, v, o, heads=H, causal=CAUSAL)
+    else:
+        a, b = (torch.randn(8192, 8192, device="cuda").bfloat16() for _ in range(2))
+        c = torch.empty_like(a)
+        for _ in range(3):
+            evk.matmul(a, b, c)
+    torch.cuda.synchronize()
+    evk.check_device_error()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -195,10 +216,14 @@ def main():
     ap.add_argument("--impl", default="evk_b200", choices=["evk_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true")
+    ap.add_argument("--profile-leg", choices=["flash", "gemm"], default=None,
+                    help="run a few launches of one leg and exit (for ncu captures; prints no JSON)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.profile_leg:
+        return profile_leg(args.profile_leg)
 
     import torch
 

@@ -61,26 +61,57 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+// Packed fp32x2 arithmetic (sm_100): two lanes of work per issued instruction.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+          "l"(*reinterpret_cast<uint64_t*>(&c)));
+    return *reinterpret_cast<float2*>(&d);
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;"
+        : "=l"(d)
+        : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+    return *reinterpret_cast<float2*>(&d);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, const Vec8& v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.w[0]), "r"(v.w[1]), "r"(v.w[2]),
+                 "r"(v.w[3])
+                 : "memory");
+}
+
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// One CTA = NT consecutive 128-query tiles of one (batch, head).
-//   warp 0       TMA producer: Q tiles once, then K_j / V_j blocks into a
-//                STAGES-deep ring (separate K and V barriers).
-//   warp 1       TMEM owner + MMA issuer.  For each block j: S_t(j) = Q_t K_j^T
-//                for every tile (S_t(j) may start as soon as softmax t has
-//                read S_t(j-1) into registers), then O_t += P_t(j-1) V_{j-1}
-//                accumulated in TMEM.
+// Persistent kernel: one CTA per SM walks work items in zig-zag rounds
+// (see item_of); an item is NT consecutive 128-query tiles of
+// one (batch, head), heaviest causal items first.  Barriers, TMEM and the
+// K/V ring live for the whole kernel, so the next item's Q and K/V loads
+// overlap the current item's last blocks and epilogue.
+//   warp 0       TMA producer: per item, Q tiles (once the previous item's S
+//                MMAs are done: q_empty), then K_j / V_j into a STAGES ring
+//                whose index runs across items.
+//   warp 1       TMEM owner + MMA issuer, event-driven per tile: S_t(j) =
+//                Q_t K_j^T once K_j is loaded and softmax t has read S_t(j-1);
+//                O_t += P_t(j) V_j once P_t(j) is written (the first PV of an
+//                item also waits until the previous item's O_t was read out).
 //   warps 2-3    idle.
 //   warpgroup 1+t  softmax of tile t, one thread per query row (= TMEM lane):
-//                one TMEM load of the S row, row max, lazy rescale of the O row
-//                in TMEM (only when the running max grows by > 2^8), P = exp2
-//                into shared memory (128-byte-swizzled K-major, the A operand
-//                of the PV MMA), finally O / l from TMEM to global memory.
+//                one TMEM load of the S row, row max, P = exp2 into shared
+//                memory (128-byte-swizzled K-major, the A operand of the PV
+//                MMA), lazy rescale of the O row in TMEM only when the running
+//                max grows by > 2^8, finally O / l from TMEM to global memory.
+// Every barrier is waited on (or probed) for exactly one completion at a time,
+// and each barrier's next completion depends on the waiter having acted, so
+// parity waits are unambiguous across items.
 template <typename T, int DH, int NT>
 __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
     flash_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, T* __restrict__ O, uint32_t N, uint32_t H,
-                    uint32_t Hkv, float scale_log2, int causal, uint32_t idesc_s, uint32_t idesc_pv,
+                    uint32_t Hkv, uint32_t BH, float scale_log2, int causal, uint32_t idesc_s, uint32_t idesc_pv,
                     unsigned int* err) {
     using Cfg = FlashCfg<DH, NT>;
     constexpr int ST = Cfg::STAGES;
@@ -92,33 +123,47 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
     uint8_t* sV = smem + Cfg::OFF_V;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
     uint64_t* q_full = bars;
-    uint64_t* k_full = q_full + 1;      // [ST]
+    uint64_t* q_empty = q_full + 1;
+    uint64_t* k_full = q_empty + 1;     // [ST]
     uint64_t* v_full = k_full + ST;     // [ST]
     uint64_t* kv_empty = v_full + ST;   // [ST]
     uint64_t* s_full = kv_empty + ST;   // [NT]
     uint64_t* s_free = s_full + NT;     // [NT]
     uint64_t* p_full = s_free + NT;     // [NT]
     uint64_t* pv_done = p_full + NT;    // [NT]
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(pv_done + NT);
+    uint64_t* o_free = pv_done + NT;    // [NT]
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(o_free + NT);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const uint32_t bh = blockIdx.x;
-    const uint32_t b = bh / H, h = bh % H;
-    const uint32_t g = h / (H / Hkv);
-    const uint32_t grp = gridDim.y - 1 - blockIdx.y;  // heaviest causal tiles first
     const uint32_t kv_all = (N + FN - 1) / FN;
-    uint32_t q0[NT], nblk[NT], nmax = 0;
+    const uint32_t qtiles = (N + FM - 1) / FM;
+    const uint32_t ngroups = (qtiles + NT - 1) / NT;
+    const uint32_t items = ngroups * BH;
+    // Work item -> (b, h, q0[t], nblk[t]); groups ordered heaviest first.
+    auto item_geom = [&](uint32_t w, uint32_t& b, uint32_t& h, uint32_t (&q0)[NT], uint32_t (&nblk)[NT]) {
+        const uint32_t grp = ngroups - 1 - w / BH;
+        const uint32_t bh = w % BH;
+        b = bh / H;
+        h = bh % H;
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-        q0[t] = (grp * NT + t) * FM;
-        nblk[t] = q0[t] < N ? (causal ? min(kv_all, q0[t] / FN + 1) : kv_all) : 0;
-        nmax = max(nmax, nblk[t]);
-    }
+        for (int t = 0; t < NT; ++t) {
+            q0[t] = (grp * NT + t) * FM;
+            nblk[t] = q0[t] < N ? (causal ? min(kv_all, q0[t] / FN + 1) : kv_all) : 0;
+        }
+    };
+
+    // Round rd of this CTA takes item rd*G + (c or G-1-c, alternating): a
+    // zig-zag over the heaviest-first order keeps the per-CTA sums of causal
+    // work within a few percent of each other.
+    auto item_of = [&](uint32_t rd) -> uint32_t {
+        return rd * gridDim.x + ((rd & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x);
+    };
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
         for (int s = 0; s < ST; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&v_full[s], 1);
@@ -129,6 +174,7 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
             mbar_init(&s_free[t], 4);
             mbar_init(&p_full[t], 4);
             mbar_init(&pv_done[t], 1);
+            mbar_init(&o_free[t], 4);
         }
         *s_abort = 0;
         fence_barrier_init();
@@ -148,203 +194,309 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
     if (warp == 0) {
         // ------------------------------------------------ TMA producer ----
         if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, NT * Cfg::Q_BYTES);
+            uint32_t r = 0, it = 0;  // ring index and item count across items
+            bool ok = true;
+            for (uint32_t rd = 0; ok && rd * gridDim.x < items; ++rd) {
+                const uint32_t w = item_of(rd);
+                if (w >= items) continue;
+                uint32_t b, h, q0[NT], nblk[NT];
+                item_geom(w, b, h, q0, nblk);
+                uint32_t nmax = 0;
 #pragma unroll
-            for (int t = 0; t < NT; ++t)
+                for (int t = 0; t < NT; ++t) nmax = max(nmax, nblk[t]);
+                const uint32_t g = h / (H / Hkv);
+                // Q buffer is free once the previous item's S MMAs completed.
+                if (it > 0 && !mbar_wait(q_empty, (it - 1) & 1, s_abort, err, kTimeoutFlash)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_expect_tx(q_full, NT * Cfg::Q_BYTES);
 #pragma unroll
-                for (int c = 0; c < DH / 64; ++c)
-                    tma_load_3d(sQ + t * Cfg::Q_BYTES + c * FM * 128, &tmQ, q_full, (int)(h * DH + c * 64), (int)q0[t],
-                                (int)b);
-            for (uint32_t j = 0; j < nmax; ++j) {
-                const int st = j % ST;
-                if (!mbar_wait(&kv_empty[st], ((j / ST) & 1) ^ 1, s_abort, err, kTimeoutFlash)) break;
-                mbar_arrive_expect_tx(&k_full[st], Cfg::KV_BYTES);
+                for (int t = 0; t < NT; ++t)
 #pragma unroll
-                for (int c = 0; c < DH / 64; ++c)
-                    tma_load_3d(sK + st * Cfg::KV_BYTES + c * FN * 128, &tmK, &k_full[st], (int)(g * DH + c * 64),
-                                (int)(j * FN), (int)b);
-                mbar_arrive_expect_tx(&v_full[st], Cfg::KV_BYTES);
+                    for (int c = 0; c < DH / 64; ++c)
+                        tma_load_3d(sQ + t * Cfg::Q_BYTES + c * FM * 128, &tmQ, q_full, (int)(h * DH + c * 64),
+                                    (int)q0[t], (int)b);
+                ++it;
+                for (uint32_t j = 0; j < nmax; ++j, ++r) {
+                    const int st = r % ST;
+                    if (!mbar_wait(&kv_empty[st], ((r / ST) & 1) ^ 1, s_abort, err, kTimeoutFlash)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&k_full[st], Cfg::KV_BYTES);
 #pragma unroll
-                for (int c = 0; c < DH / 64; ++c)
-                    tma_load_3d(sV + st * Cfg::KV_BYTES + c * FN * 128, &tmV, &v_full[st], (int)(g * DH + c * 64),
-                                (int)(j * FN), (int)b);
+                    for (int c = 0; c < DH / 64; ++c)
+                        tma_load_3d(sK + st * Cfg::KV_BYTES + c * FN * 128, &tmK, &k_full[st], (int)(g * DH + c * 64),
+                                    (int)(j * FN), (int)b);
+                    mbar_arrive_expect_tx(&v_full[st], Cfg::KV_BYTES);
+#pragma unroll
+                    for (int c = 0; c < DH / 64; ++c)
+                        tma_load_3d(sV + st * Cfg::KV_BYTES + c * FN * 128, &tmV, &v_full[st], (int)(g * DH + c * 64),
+                                    (int)(j * FN), (int)b);
+                }
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------- MMA issuer ----
         if (lane == 0) {
-            bool ok = mbar_wait(q_full, 0, s_abort, err, kTimeoutFlash);
-            tc_fence_after();
             const uint32_t qaddr = smem_u32(sQ);
             const uint32_t paddr = smem_u32(sP);
-            auto issue_pv = [&](uint32_t jj) -> bool {
-                const int st = jj % ST;
-                if (!mbar_wait(&v_full[st], (jj / ST) & 1, s_abort, err, kTimeoutFlash)) return false;
-                const uint32_t vaddr = smem_u32(sV + st * Cfg::KV_BYTES);
+            uint32_t rbase = 0, it = 0;
+            uint32_t gs[NT], ep[NT];  // per tile: blocks processed before this item, epilogues finished
 #pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    if (jj >= nblk[t]) continue;
-                    if (!mbar_wait(&p_full[t], jj & 1, s_abort, err, kTimeoutFlash)) return false;
-                    tc_fence_after();
+            for (int t = 0; t < NT; ++t) gs[t] = ep[t] = 0;
+            bool ok = true;
+            long long idle_since = clock64();
+            for (uint32_t rd = 0; ok && rd * gridDim.x < items; ++rd) {
+                const uint32_t w = item_of(rd);
+                if (w >= items) continue;
+                uint32_t b, h, q0[NT], nblk[NT];
+                item_geom(w, b, h, q0, nblk);
+                uint32_t nmax = 0;
 #pragma unroll
-                    for (int kk = 0; kk < FN / 16; ++kk) {
-                        uint64_t ad = make_sw128_desc(paddr + t * Cfg::P_BYTES + (kk >> 2) * (FM * 128) + (kk & 3) * 32,
-                                                      16, 1024);
-                        uint64_t bd = make_sw128_desc(vaddr + kk * 2048, FN * 128, 1024);
-                        mma_f16_ss(tmem + Cfg::col_o(t), ad, bd, idesc_pv, (jj | kk) != 0);
+                for (int t = 0; t < NT; ++t) nmax = max(nmax, nblk[t]);
+                if (!mbar_wait(q_full, it & 1, s_abort, err, kTimeoutFlash)) break;
+                tc_fence_after();
+                uint32_t ns[NT], np[NT];
+#pragma unroll
+                for (int t = 0; t < NT; ++t) ns[t] = np[t] = 0;
+                uint32_t released = 0;
+                bool q_released = false;
+                while (true) {
+                    bool done = true, progress = false;
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        if (np[t] < nblk[t]) done = false;
+                        const uint32_t j = ns[t];
+                        const uint32_t gj = gs[t] + j;  // tile-global block index
+                        if (j < nblk[t] && mbar_try_wait(smem_u32(&k_full[(rbase + j) % ST]), ((rbase + j) / ST) & 1) &&
+                            (gj == 0 || mbar_try_wait(smem_u32(&s_free[t]), (gj - 1) & 1))) {
+                            tc_fence_after();
+                            const uint32_t kaddr = smem_u32(sK + ((rbase + j) % ST) * Cfg::KV_BYTES);
+#pragma unroll
+                            for (int kk = 0; kk < DH / 16; ++kk) {
+                                uint64_t ad = make_sw128_desc(
+                                    qaddr + t * Cfg::Q_BYTES + (kk >> 2) * (FM * 128) + (kk & 3) * 32, 16, 1024);
+                                uint64_t bd = make_sw128_desc(kaddr + (kk >> 2) * (FN * 128) + (kk & 3) * 32, 16, 1024);
+                                mma_f16_ss(tmem + Cfg::col_s(t), ad, bd, idesc_s, kk != 0);
+                            }
+                            mma_commit(&s_full[t]);
+                            ns[t] = j + 1;
+                            progress = true;
+                        }
+                        const uint32_t jj = np[t];
+                        const uint32_t gjj = gs[t] + jj;
+                        if (jj < ns[t] && mbar_try_wait(smem_u32(&p_full[t]), gjj & 1) &&
+                            mbar_try_wait(smem_u32(&v_full[(rbase + jj) % ST]), ((rbase + jj) / ST) & 1) &&
+                            (jj != 0 || ep[t] == 0 || mbar_try_wait(smem_u32(&o_free[t]), (ep[t] - 1) & 1))) {
+                            tc_fence_after();
+                            const uint32_t vaddr = smem_u32(sV + ((rbase + jj) % ST) * Cfg::KV_BYTES);
+#pragma unroll
+                            for (int kk = 0; kk < FN / 16; ++kk) {
+                                uint64_t ad = make_sw128_desc(
+                                    paddr + t * Cfg::P_BYTES + (kk >> 2) * (FM * 128) + (kk & 3) * 32, 16, 1024);
+                                uint64_t bd = make_sw128_desc(vaddr + kk * 2048, FN * 128, 1024);
+                                mma_f16_ss(tmem + Cfg::col_o(t), ad, bd, idesc_pv, (jj | kk) != 0);
+                            }
+                            mma_commit(&pv_done[t]);
+                            np[t] = jj + 1;
+                            progress = true;
+                        }
                     }
-                    mma_commit(&pv_done[t]);
-                }
-                mma_commit(&kv_empty[st]);
-                return true;
-            };
-            for (uint32_t j = 0; ok && j < nmax; ++j) {
-                const int st = j % ST;
-                if (!mbar_wait(&k_full[st], (j / ST) & 1, s_abort, err, kTimeoutFlash)) break;
-                const uint32_t kaddr = smem_u32(sK + st * Cfg::KV_BYTES);
+                    // Q is free once every S of this item has been issued (the
+                    // commit fires when those MMAs have completed).
+                    if (!q_released) {
+                        bool all_s = true;
 #pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    if (j >= nblk[t]) continue;
-                    if (j >= 1 && !mbar_wait(&s_free[t], (j - 1) & 1, s_abort, err, kTimeoutFlash)) {
+                        for (int t = 0; t < NT; ++t) all_s = all_s && ns[t] == nblk[t];
+                        if (all_s) {
+                            mma_commit(q_empty);
+                            q_released = true;
+                        }
+                    }
+                    // Hand back ring slots whose block every tile has consumed.
+                    while (released < nmax) {
+                        bool all = true;
+#pragma unroll
+                        for (int t = 0; t < NT; ++t)
+                            if (released < nblk[t] && np[t] <= released) all = false;
+                        if (!all) break;
+                        mma_commit(&kv_empty[(rbase + released) % ST]);
+                        ++released;
+                    }
+                    if (done) break;
+                    if (progress) {
+                        idle_since = clock64();
+                    } else if (*s_abort || *reinterpret_cast<volatile unsigned int*>(err)) {
+                        *s_abort = 1;
                         ok = false;
                         break;
+                    } else if (clock64() - idle_since > kSpinLimitCycles) {
+                        *s_abort = 1;
+                        atomicCAS(err, 0u, kTimeoutFlash);
+                        ok = false;
+                        break;
+                    } else {
+                        __nanosleep(32);  // leave issue slots to the softmax warps on this scheduler
                     }
-                    tc_fence_after();
-#pragma unroll
-                    for (int kk = 0; kk < DH / 16; ++kk) {
-                        uint64_t ad = make_sw128_desc(qaddr + t * Cfg::Q_BYTES + (kk >> 2) * (FM * 128) + (kk & 3) * 32,
-                                                      16, 1024);
-                        uint64_t bd = make_sw128_desc(kaddr + (kk >> 2) * (FN * 128) + (kk & 3) * 32, 16, 1024);
-                        mma_f16_ss(tmem + Cfg::col_s(t), ad, bd, idesc_s, kk != 0);
-                    }
-                    mma_commit(&s_full[t]);
                 }
-                if (ok && j >= 1 && !issue_pv(j - 1)) ok = false;
+                ++it;
+                rbase += nmax;
+#pragma unroll
+                for (int t = 0; t < NT; ++t) {
+                    gs[t] += nblk[t];
+                    if (nblk[t] > 0) ++ep[t];
+                }
             }
-            if (ok && nmax > 0) issue_pv(nmax - 1);
         }
     } else if (warp >= 4) {
         // --------------------------------------------- softmax warps ----
         const int t = (warp >> 2) - 1;
         const int quarter = warp & 3;
         const uint32_t row = quarter * 32 + lane;  // TMEM lane == query row in the tile
-        const uint32_t qidx = q0[t] + row;
         const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
         const uint32_t s_addr = lane_addr + Cfg::col_s(t);
         const uint32_t o_addr = lane_addr + Cfg::col_o(t);
-        const uint32_t kmax = min(N, causal ? qidx + 1 : N);  // keys < kmax are valid
-        uint8_t* prow = sP + t * Cfg::P_BYTES + row * 128;
-        float m_ref = -INFINITY, l = 0.0f;
+        const uint32_t prow = smem_u32(sP + t * Cfg::P_BYTES + row * 128);
+        uint32_t gbase = 0;  // blocks this tile processed in earlier items
         bool ok = true;
-        const uint32_t nb = nblk[t];
-        for (uint32_t j = 0; j < nb; ++j) {
-            if (!mbar_wait(&s_full[t], j & 1, s_abort, err, kTimeoutFlash)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            uint32_t sr[FN / 32][32];
-#pragma unroll
-            for (int c = 0; c < FN / 32; ++c) tmem_ld32(s_addr + c * 32, sr[c]);
-            tmem_wait_ld();
-            // S is in registers: the tensor core may overwrite it with S_t(j+1).
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[t]);
-
-            const uint32_t k0 = j * FN;
-            const bool need_mask = (k0 + FN > N) || (causal && j + 1 == nb);
-            float mx = -INFINITY;
-            if (need_mask) {
-#pragma unroll
-                for (int c = 0; c < FN / 32; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        if (k0 + c * 32 + e >= kmax) sr[c][e] = __float_as_uint(-INFINITY);
-                        mx = fmaxf(mx, __uint_as_float(sr[c][e]));
-                    }
-            } else {
-#pragma unroll
-                for (int c = 0; c < FN / 32; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) mx = fmaxf(mx, __uint_as_float(sr[c][e]));
-            }
-            const float m_cand = fmaxf(m_ref, mx * scale_log2);
-            // Lazy rescale: keep the reference max unless it grew by > 2^8.
-            const bool need = j > 0 && m_cand > m_ref + kRescaleThreshold;
-            const float alpha = need ? ex2(m_ref - m_cand) : 1.0f;  // m_ref = -inf -> 0
-            if (j == 0 || need) m_ref = m_cand;
-            if (j > 0) {
-                // PV_t(j-1) must be complete before the P buffer is reused
-                // and before O is rescaled.
-                if (!mbar_wait(&pv_done[t], (j - 1) & 1, s_abort, err, kTimeoutFlash)) {
+        for (uint32_t rd = 0; ok && rd * gridDim.x < items; ++rd) {
+            const uint32_t w = item_of(rd);
+            if (w >= items) continue;
+            uint32_t b, h, q0[NT], nblk[NT];
+            item_geom(w, b, h, q0, nblk);
+            const uint32_t nb = nblk[t];
+            if (nb == 0) continue;
+            const uint32_t qidx = q0[t] + row;
+            const uint32_t kmax = min(N, causal ? qidx + 1 : N);  // keys < kmax are valid
+            float m_ref = -INFINITY, l = 0.0f;
+            for (uint32_t j = 0; j < nb; ++j) {
+                const uint32_t gj = gbase + j;
+                if (!mbar_wait(&s_full[t], gj & 1, s_abort, err, kTimeoutFlash)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-            }
-            const float m_use = (m_ref == -INFINITY) ? 0.0f : m_ref;
-            float rs = 0.0f;
+                uint32_t sr[FN / 32][32];
 #pragma unroll
-            for (int c = 0; c < FN / 32; ++c) {
+                for (int c = 0; c < FN / 32; ++c) tmem_ld32(s_addr + c * 32, sr[c]);
+                tmem_wait_ld();
+                // S is in registers: the tensor core may overwrite it with S_t(j+1).
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[t]);
+
+                const uint32_t k0 = j * FN;
+                const bool need_mask = (k0 + FN > N) || (causal && j + 1 == nb);
+                // Row max with 8 independent accumulators.
+                float mxa[8];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    float f[8];
+                for (int i = 0; i < 8; ++i) mxa[i] = -INFINITY;
+                if (need_mask) {
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        // masked entries hold -inf: exp2(-inf) = 0
-                        f[e] = ex2(fmaf(__uint_as_float(sr[c][q * 8 + e]), scale_log2, -m_use));
-                        rs += f[e];
+                    for (int c = 0; c < FN / 32; ++c)
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            if (k0 + c * 32 + e >= kmax) sr[c][e] = __float_as_uint(-INFINITY);
+                            mxa[e & 7] = fmaxf(mxa[e & 7], __uint_as_float(sr[c][e]));
+                        }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < FN / 32; ++c)
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) mxa[e & 7] = fmaxf(mxa[e & 7], __uint_as_float(sr[c][e]));
+                }
+                const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
+                                       fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+                const float m_cand = fmaxf(m_ref, mx * scale_log2);
+                // Lazy rescale: keep the reference max unless it grew by > 2^8.
+                const bool need = j > 0 && m_cand > m_ref + kRescaleThreshold;
+                const float alpha = need ? ex2(m_ref - m_cand) : 1.0f;  // m_ref = -inf -> 0
+                if (j == 0 || need) m_ref = m_cand;
+                if (j > 0) {
+                    // PV_t(j-1) must be complete before the P buffer is reused
+                    // and before O is rescaled.
+                    if (!mbar_wait(&pv_done[t], (gj - 1) & 1, s_abort, err, kTimeoutFlash)) {
+                        ok = false;
+                        break;
                     }
-                    const int key = c * 32 + q * 8;
-                    const int chunk = (key & 63) >> 3;
-                    *reinterpret_cast<Vec8*>(prow + (key >> 6) * (FM * 128) + ((chunk ^ (row & 7)) << 4)) =
-                        pack8<T>(f);
+                    tc_fence_after();
+                }
+                const float m_use = (m_ref == -INFINITY) ? 0.0f : m_ref;
+                // p = exp2(s * scale_log2 - m) with packed fp32x2 scale-subtract and sums.
+                const float2 sc2 = make_float2(scale_log2, scale_log2);
+                const float2 nm2 = make_float2(-m_use, -m_use);
+                float2 rs2[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) rs2[i] = make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int c = 0; c < FN / 32; ++c) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float f[8];
+#pragma unroll
+                        for (int e = 0; e < 8; e += 2) {
+                            // masked entries hold -inf: exp2(-inf) = 0
+                            float2 x = ffma2(make_float2(__uint_as_float(sr[c][q * 8 + e]),
+                                                         __uint_as_float(sr[c][q * 8 + e + 1])), sc2, nm2);
+                            f[e] = ex2(x.x);
+                            f[e + 1] = ex2(x.y);
+                            rs2[e >> 1] = fadd2(rs2[e >> 1], make_float2(f[e], f[e + 1]));
+                        }
+                        const int key = c * 32 + q * 8;
+                        const int chunk = (key & 63) >> 3;
+                        st_shared_v4(prow + (key >> 6) * (FM * 128) + ((chunk ^ (row & 7)) << 4), pack8<T>(f));
+                    }
+                }
+                const float rs = ((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y)) +
+                                 ((rs2[2].x + rs2[2].y) + (rs2[3].x + rs2[3].y));
+                l = l * alpha + rs;
+                if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+                    for (int c = 0; c < DH / 32; ++c) {
+                        uint32_t rr[32];
+                        tmem_ld32(o_addr + c * 32, rr);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+                        tmem_st32(o_addr + c * 32, rr);
+                    }
+                    tmem_wait_st();
+                }
+                // P (shared-memory stores) and any O rescale must be visible to
+                // the tensor core before the PV MMA is issued.
+                fence_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[t]);
+            }
+            if (!ok) break;
+            // Epilogue: O / l from TMEM to global memory, then O_t is free.
+            const uint32_t glast = gbase + nb - 1;
+            if (!mbar_wait(&pv_done[t], glast & 1, s_abort, err, kTimeoutFlash)) break;
+            tc_fence_after();
+            const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+            T* orow = O + ((uint64_t)b * N + qidx) * ((uint64_t)H * DH) + (uint64_t)h * DH;
+#pragma unroll
+            for (int c = 0; c < DH / 32; ++c) {
+                uint32_t rr[32];
+                tmem_ld32(o_addr + c * 32, rr);
+                tmem_wait_ld();
+                if (qidx < N) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        float f[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(rr[q * 8 + e]) * inv;
+                        reinterpret_cast<Vec8*>(orow + c * 32)[q] = pack8<T>(f);
+                    }
                 }
             }
-            l = l * alpha + rs;
-            if (__any_sync(0xffffffffu, need)) {
-#pragma unroll
-                for (int c = 0; c < DH / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld32(o_addr + c * 32, r);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-                    tmem_st32(o_addr + c * 32, r);
-                }
-                tmem_wait_st();
-            }
-            // P (generic-proxy stores) and any O rescale must be visible to the
-            // tensor core before the PV MMA is issued.
-            fence_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[t]);
-        }
-        if (ok && nb > 0) {
-            ok = mbar_wait(&pv_done[t], (nb - 1) & 1, s_abort, err, kTimeoutFlash);
-            tc_fence_after();
-            if (ok) {
-                const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-                T* orow = O + ((uint64_t)b * N + qidx) * ((uint64_t)H * DH) + (uint64_t)h * DH;
-#pragma unroll
-                for (int c = 0; c < DH / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld32(o_addr + c * 32, r);
-                    tmem_wait_ld();
-                    if (qidx < N) {
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            float f[8];
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[q * 8 + e]) * inv;
-                            reinterpret_cast<Vec8*>(orow + c * 32)[q] = pack8<T>(f);
-                        }
-                    }
-                }
-            }
-            tc_fence_before();
+            if (lane == 0) mbar_arrive(&o_free[t]);
+            gbase += nb;
         }
     }
     __syncthreads();
@@ -428,9 +580,10 @@ int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32
     const uint32_t idesc_s = make_idesc_f16(FM, FN, bf, 0, 0);
     const uint32_t idesc_pv = make_idesc_f16(FM, DH, bf, 0, 1);
     const uint32_t qtiles = (N + FM - 1) / FM;
-    dim3 grid(B * H, (qtiles + NT - 1) / NT);
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(mQ, mK, mV, (T*)o, N, H, Hkv, scale_log2, causal, idesc_s, idesc_pv,
-                                                state()->d_error);
+    const uint64_t items = (uint64_t)B * H * ((qtiles + NT - 1) / NT);
+    const unsigned grid = (unsigned)std::min<uint64_t>(items, (uint64_t)state()->sm_count);
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(mQ, mK, mV, (T*)o, N, H, Hkv, B * H, scale_log2, causal, idesc_s,
+                                                idesc_pv, state()->d_error);
     return after_launch("evkcu_flash_attention(tcgen05)");
 }
 
