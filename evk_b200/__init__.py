@@ -281,3 +281,96 @@ def greedy_sample(logits, out, position, token_base, token_count, stream=None):
         _ptr(logits), _ptr(out), B, S, V, position, token_base, token_count, ob, _dtype_code(logits),
         _stream(stream)))
     return out
+
+
+# ------------------------------------------------------------- LLM driver --
+class LlmConfig(ctypes.Structure):
+    """evkcu_llm_config (include/evkcu.h)."""
+
+    _fields_ = [(n, ctypes.c_uint32) for n in ("layers", "d_model", "heads", "kv_heads", "hidden", "vocab",
+                                                "max_batch", "max_seq")] + \
+               [("rope_base", ctypes.c_float), ("eps", ctypes.c_float), ("dtype", ctypes.c_int),
+                ("tied_embeddings", ctypes.c_uint32), ("tp_rank", ctypes.c_uint32), ("tp_size", ctypes.c_uint32)]
+
+
+_pp = ctypes.POINTER(ctypes.c_void_p)
+SIGNATURES.update({
+    "evkcu_single_query_attention_devlen": [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _vp, _f32, _int, _vp],
+    "evkcu_comm_unique_id": [_vp],
+    "evkcu_comm_init": [_vp, _int, _int, _pp],
+    "evkcu_comm_destroy": [_vp],
+    "evkcu_llm_create": [ctypes.POINTER(LlmConfig), _vp, _pp],
+    "evkcu_llm_destroy": [_vp],
+    "evkcu_llm_init_random": [_vp, _u64, _f32, _vp],
+    "evkcu_llm_set_weight": [_vp, ctypes.c_char_p, _u32, _vp, _vp],
+    "evkcu_llm_prefill": [_vp, _vp, _u32, _u32, _vp, _vp, _vp],
+    "evkcu_llm_decode": [_vp, _vp, _vp, _vp, _vp],
+    "evkcu_llm_length": [_vp],
+})
+_RET["evkcu_llm_length"] = ctypes.c_uint32
+
+
+class Comm:
+    """NCCL communicator for tensor parallelism (one process per GPU)."""
+
+    def __init__(self, unique_id: bytes, rank: int, world: int):
+        self.handle = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(unique_id, 128)
+        _check("evkcu_comm_init", lib().evkcu_comm_init(buf, rank, world, ctypes.byref(self.handle)))
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        _check("evkcu_comm_unique_id", lib().evkcu_comm_unique_id(buf))
+        return buf.raw
+
+    def close(self):
+        if self.handle:
+            _check("evkcu_comm_destroy", lib().evkcu_comm_destroy(self.handle))
+            self.handle = ctypes.c_void_p()
+
+
+class Llm:
+    """Device-resident decoder (evkcu_llm_*): prefill, CUDA-graph decode,
+    optional tensor parallelism.  Token ids are int32 CUDA tensors."""
+
+    def __init__(self, layers, d_model, heads, hidden, vocab, max_batch, max_seq, kv_heads=None, rope_base=10000.0,
+                 eps=1e-5, dtype=F16, tied_embeddings=True, tp_rank=0, tp_size=1, comm: Optional[Comm] = None):
+        self.cfg = LlmConfig(layers, d_model, heads, kv_heads or heads, hidden, vocab, max_batch, max_seq, rope_base,
+                             eps, dtype, int(tied_embeddings), tp_rank, tp_size)
+        self.handle = ctypes.c_void_p()
+        _check("evkcu_llm_create", lib().evkcu_llm_create(ctypes.byref(self.cfg), comm.handle if comm else None,
+                                                          ctypes.byref(self.handle)))
+
+    def close(self):
+        if self.handle:
+            lib().evkcu_llm_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def init_random(self, seed=42, std=0.02, stream=None):
+        _check("evkcu_llm_init_random", lib().evkcu_llm_init_random(self.handle, seed, std, _stream(stream)))
+
+    def set_weight(self, name: str, tensor, layer: int = 0, stream=None):
+        _check("evkcu_llm_set_weight", lib().evkcu_llm_set_weight(self.handle, name.encode(), layer, _ptr(tensor),
+                                                                  _stream(stream)))
+
+    def prefill(self, tokens, next_ids, logits=None, stream=None):
+        B, S = tokens.shape
+        _check("evkcu_llm_prefill", lib().evkcu_llm_prefill(self.handle, _ptr(tokens), B, S, _ptr(next_ids),
+                                                            _ptr(logits), _stream(stream)))
+        return next_ids
+
+    def decode(self, ids, next_ids, logits=None, stream=None):
+        _check("evkcu_llm_decode", lib().evkcu_llm_decode(self.handle, _ptr(ids), _ptr(next_ids), _ptr(logits),
+                                                          _stream(stream)))
+        return next_ids
+
+    @property
+    def length(self) -> int:
+        return int(lib().evkcu_llm_length(self.handle))

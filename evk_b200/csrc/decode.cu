@@ -38,7 +38,8 @@ __device__ __forceinline__ float ex2f(float x) {
 template <typename T, int LPK>
 __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc, T* __restrict__ out, uint32_t H,
-    uint32_t Hkv, uint32_t Dh, uint32_t max_len, uint32_t cur_len, uint32_t chunk, float scale_log2,
+    uint32_t Hkv, uint32_t Dh, uint32_t max_len, uint32_t cur_len, const uint32_t* __restrict__ d_cur_len,
+    uint32_t chunk, float scale_log2,
     float* __restrict__ partial, unsigned int* __restrict__ tickets) {
     constexpr int KPW = 32 / LPK;  // rows per warp iteration
     constexpr int NW = kDecThreads / 32;
@@ -81,7 +82,10 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
         for (int e = 0; e < 8; ++e) o[i][e] = 0.0f;
     }
     const uint32_t pbeg = split * chunk;
-    const uint32_t pend = min(pbeg + chunk, cur_len);
+    // With d_cur_len the length lives in device memory (the grid was sized for
+    // max_len), so a captured graph can replay with a growing cache.
+    const uint32_t len = d_cur_len ? min(*d_cur_len, max_len) : cur_len;
+    const uint32_t pend = min(pbeg + chunk, len);
     const uint64_t row_pitch = (uint64_t)Hkv * Dh;
     const T* kbase = kc + (uint64_t)b * max_len * row_pitch + (uint64_t)g * Dh + d0;
     const T* vbase = vc + (uint64_t)b * max_len * row_pitch + (uint64_t)g * Dh + d0;
@@ -197,7 +201,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
 
 template <typename T, int LPK>
 int launch_decode(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t H, uint32_t Hkv,
-                  uint32_t Dh, uint32_t max_len, uint32_t cur_len, float scale_log2, cudaStream_t st) {
+                  uint32_t Dh, uint32_t max_len, uint32_t cur_len, const uint32_t* d_cur_len, float scale_log2,
+                  cudaStream_t st) {
     DeviceState* ds = state();
     const uint32_t Gq = H / Hkv;
     const uint32_t hgroups = (Gq + kMaxGroup - 1) / kMaxGroup;
@@ -214,7 +219,8 @@ int launch_decode(const void* q, const void* k, const void* v, void* o, uint32_t
     if (!ws) return fail(EVKCU_CUDA_ERROR, "evkcu_single_query_attention: scratch allocation failed");
     dim3 grid(nsplit, Hkv * hgroups, B);
     decode_attn_kernel<T, LPK><<<grid, kDecThreads, 0, st>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, H, Hkv, Dh,
-                                                            max_len, cur_len, chunk, scale_log2, (float*)(ws + toff),
+                                                            max_len, cur_len, d_cur_len, chunk, scale_log2,
+                                                            (float*)(ws + toff),
                                                             (unsigned int*)ws);
     return after_launch("evkcu_single_query_attention");
 }
@@ -245,10 +251,36 @@ extern "C" int evkcu_single_query_attention(const void* q, const void* kcache, c
     const float sl2 = scale * 1.4426950408889634f;
     const uint32_t slices = Dh / 8;
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-        if (slices <= 2) return launch_decode<T, 2>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, cur_len, sl2, st);
-        if (slices <= 4) return launch_decode<T, 4>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, cur_len, sl2, st);
-        if (slices <= 8) return launch_decode<T, 8>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, cur_len, sl2, st);
-        if (slices <= 16) return launch_decode<T, 16>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, cur_len, sl2, st);
-        return launch_decode<T, 32>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, cur_len, sl2, st);
+        if (slices <= 2) return launch_decode<T, 2>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, cur_len, nullptr, sl2, st);
+        if (slices <= 4) return launch_decode<T, 4>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, cur_len, nullptr, sl2, st);
+        if (slices <= 8) return launch_decode<T, 8>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, cur_len, nullptr, sl2, st);
+        if (slices <= 16) return launch_decode<T, 16>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, cur_len, nullptr, sl2, st);
+        return launch_decode<T, 32>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, cur_len, nullptr, sl2, st);
+    });
+}
+
+extern "C" int evkcu_single_query_attention_devlen(const void* q, const void* kcache, const void* vcache, void* out,
+                                                   uint32_t B, uint32_t H, uint32_t Hkv, uint32_t Dh,
+                                                   uint32_t max_len, const uint32_t* d_cur_len, float scale, int dtype,
+                                                   void* stream) {
+    if (B == 0 || H == 0) return EVKCU_OK;
+    EVKCU_CHECK_ARG(q && kcache && vcache && out && d_cur_len, EVKCU_BAD_ARG,
+                    "evkcu_single_query_attention_devlen: null pointer");
+    EVKCU_CHECK_ARG(Hkv >= 1 && H % Hkv == 0, EVKCU_BAD_SHAPE, "evkcu_single_query_attention_devlen: H % Hkv != 0");
+    EVKCU_CHECK_ARG(Dh % 8 == 0 && Dh >= 8 && Dh <= 256 && max_len > 0, EVKCU_BAD_SHAPE,
+                    "evkcu_single_query_attention_devlen: Dh must be a multiple of 8 in [8, 256], max_len > 0");
+    EVKCU_CHECK_ARG(aligned16(q) && aligned16(kcache) && aligned16(vcache) && aligned16(out), EVKCU_BAD_ALIGN,
+                    "evkcu_single_query_attention_devlen: pointers must be 16-byte aligned");
+    if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)Dh);
+    const float sl2 = scale * 1.4426950408889634f;
+    const uint32_t slices = Dh / 8;
+    cudaStream_t st = as_stream(stream);
+    const uint32_t* dl = d_cur_len;
+    return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
+        if (slices <= 2) return launch_decode<T, 2>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, max_len, dl, sl2, st);
+        if (slices <= 4) return launch_decode<T, 4>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, max_len, dl, sl2, st);
+        if (slices <= 8) return launch_decode<T, 8>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, max_len, dl, sl2, st);
+        if (slices <= 16) return launch_decode<T, 16>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, max_len, dl, sl2, st);
+        return launch_decode<T, 32>(q, kcache, vcache, out, B, H, Hkv, Dh, max_len, max_len, dl, sl2, st);
     });
 }

@@ -21,26 +21,13 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "greedy_key.cuh"
 
 namespace evkcu {
 namespace {
 
 constexpr int kThreads = 256;
 constexpr uint32_t kChunk = 4096;  // window elements per CTA
-
-__device__ __forceinline__ uint64_t elem_key(float v, uint32_t j) {
-    if (!(v > -FLT_MAX)) return 0ull;  // NaN, -inf: never selected
-    uint32_t u = __float_as_uint(v);
-    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-    uint32_t rank = (__brev(j & 255u) >> 24) << 24 | (j >> 8);
-    return ((uint64_t)u << 32) | (uint64_t)(0xFFFFFFFFu - rank);
-}
-
-__device__ __forceinline__ uint32_t key_to_offset(uint64_t key) {
-    uint32_t rank = 0xFFFFFFFFu - (uint32_t)key;
-    uint32_t lane = __brev(rank >> 24) >> 24;
-    return (rank & 0xFFFFFFu) * 256u + lane;
-}
 
 __device__ __forceinline__ uint64_t warp_max_u64(uint64_t k) {
 #pragma unroll

@@ -180,6 +180,72 @@ int evkcu_greedy_sample_noalloc(const void* logits, void* out, uint32_t B, uint3
                                 uint32_t position, uint32_t token_base, uint32_t token_count,
                                 uint32_t out_bytes, int dtype, void* stream);
 
+
+/* Decode attention whose cache length is read from device memory (*d_cur_len)
+ * when the kernel runs, so one captured CUDA graph can replay every decode
+ * step of a growing cache.  Otherwise as evkcu_single_query_attention; the
+ * grid is sized for max_len.  Extension (no reference counterpart).         */
+int evkcu_single_query_attention_devlen(const void* q, const void* kcache, const void* vcache, void* out,
+                                        uint32_t B, uint32_t H, uint32_t Hkv, uint32_t Dh,
+                                        uint32_t max_len, const uint32_t* d_cur_len, float scale,
+                                        int dtype, void* stream);
+
+/* ---- LLM driver (extension) ------------------------------------------------
+ * The decoder that example/main_llm.cpp builds from these operators
+ * (CausalAttentionBlock::forward :528-546, MeshTokenModel::build_graph
+ * :588-606, sample_autoregressive :622-654), as one device-resident object:
+ * pre-RMSNorm (no gain, as evk::ai::rms_norm), multi-head attention with
+ * per-head interleaved RoPE, GELU MLP, residual adds, final RMSNorm, LM head
+ * (tied to the embedding or separate), greedy sampling.  Unlike the
+ * reference's full-sequence recompute per token, decode keeps a KV cache and
+ * runs one CUDA graph per step with no host round trip.
+ * Tensor parallel (tp_size > 1, one process per GPU): attention heads and MLP
+ * columns are split across ranks, Wo / W2 outputs are summed with an NCCL
+ * all-reduce, the vocabulary is split for the LM head and greedy sampling
+ * combines the ranks' 64-bit selection keys with an all-gather.            */
+typedef struct evkcu_llm_config {
+    uint32_t layers, d_model, heads, kv_heads, hidden, vocab;
+    uint32_t max_batch, max_seq;
+    float rope_base, eps;
+    int dtype;                /* EVKCU_F16 or EVKCU_BF16 */
+    uint32_t tied_embeddings; /* 1: logits = x . embedding^T */
+    uint32_t tp_rank, tp_size;
+} evkcu_llm_config;
+
+typedef struct evkcu_llm evkcu_llm;
+
+/* NCCL communicator set-up for tensor parallelism: rank 0 creates the id, the
+ * caller distributes its 128 bytes, every rank calls evkcu_comm_init.       */
+int evkcu_comm_unique_id(void* id128);
+int evkcu_comm_init(const void* id128, int rank, int world, void** comm);
+int evkcu_comm_destroy(void* comm);
+
+/* Allocates weights, KV cache and activations on the current device.  comm is
+ * an evkcu_comm_init communicator when tp_size > 1, else NULL.              */
+int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_llm** out);
+int evkcu_llm_destroy(evkcu_llm* m);
+/* Seeded N(0, std) weights generated on the device from each element's global
+ * index, so every tensor-parallel size builds the same model.              */
+int evkcu_llm_init_random(evkcu_llm* m, uint64_t seed, float std, void* stream);
+/* Copies one full (unsharded) weight from device memory; this rank keeps its
+ * shard.  name: "embedding" [V, D], "lm_head" [D, V], and per layer "wqkv"
+ * [D, (H + 2 Hkv) Dh] (columns: q heads, k heads, v heads), "wo" [H Dh, D],
+ * "w1" [D, F], "w2" [F, D].                                                  */
+int evkcu_llm_set_weight(evkcu_llm* m, const char* name, uint32_t layer, const void* src, void* stream);
+/* Prefill: tokens [B, S] (uint32, device) -> KV cache positions 0..S-1 and
+ * the next token per sequence (next_ids [B], uint32, device).  Resets the
+ * cache.  Optionally logits_out [B, vocab] (device, storage dtype) receives
+ * the last position's logits (gathered across ranks).                      */
+int evkcu_llm_prefill(evkcu_llm* m, const uint32_t* tokens, uint32_t B, uint32_t S, uint32_t* next_ids,
+                      void* logits_out, void* stream);
+/* One decode step for the B sequences of the last prefill: consumes ids [B]
+ * (the tokens at the current position) and writes next_ids [B].  From the
+ * second step of a batch size on, replays a captured CUDA graph (needs a
+ * non-default stream and logits_out == NULL; otherwise runs eagerly).      */
+int evkcu_llm_decode(evkcu_llm* m, const uint32_t* ids, uint32_t* next_ids, void* logits_out, void* stream);
+/* Number of cached positions (prefill length + decode steps).  Host value. */
+uint32_t evkcu_llm_length(const evkcu_llm* m);
+
 #ifdef __cplusplus
 }
 #endif
