@@ -35,7 +35,7 @@ __device__ __forceinline__ float ex2f(float x) {
 }
 
 // partial layout per (b, h, split): m, l, o[Dh]  (fp32)
-template <typename T, int LPK>
+template <typename T, int LPK, int G>
 __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc, T* __restrict__ out, uint32_t H,
     uint32_t Hkv, uint32_t Dh, uint32_t max_len, uint32_t cur_len, const uint32_t* __restrict__ d_cur_len,
@@ -43,8 +43,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     float* __restrict__ partial, unsigned int* __restrict__ tickets) {
     constexpr int KPW = 32 / LPK;  // rows per warp iteration
     constexpr int NW = kDecThreads / 32;
-    __shared__ float sm_m[NW][kMaxGroup], sm_l[NW][kMaxGroup];
-    __shared__ float sm_o[NW][kMaxGroup][LPK * 8];
+    __shared__ float sm_m[NW][G], sm_l[NW][G];
+    __shared__ float sm_o[NW][G][LPK * 8];
     __shared__ bool is_last;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -52,18 +52,18 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     const int grp = lane / LPK;   // which row of the warp iteration
     const uint32_t split = blockIdx.x, nsplit = gridDim.x;
     const uint32_t Gq = H / Hkv;
-    const uint32_t hgroups = (Gq + kMaxGroup - 1) / kMaxGroup;
+    const uint32_t hgroups = (Gq + G - 1) / G;
     const uint32_t g = blockIdx.y / hgroups;
     const uint32_t hg = blockIdx.y % hgroups;
-    const uint32_t h0 = g * Gq + hg * kMaxGroup;
-    const uint32_t nh = min((uint32_t)kMaxGroup, Gq - hg * kMaxGroup);
+    const uint32_t h0 = g * Gq + hg * G;
+    const uint32_t nh = min((uint32_t)G, Gq - hg * G);
     const uint32_t b = blockIdx.z;
     const uint32_t d0 = sub * 8;
     const bool dvalid = d0 < Dh;
 
-    float qf[kMaxGroup][8];
+    float qf[G][8];
 #pragma unroll
-    for (int i = 0; i < kMaxGroup; ++i) {
+    for (int i = 0; i < G; ++i) {
         if (i < (int)nh && dvalid) {
             unpack8<T>(*reinterpret_cast<const Vec8*>(q + ((uint64_t)b * H + h0 + i) * Dh + d0), qf[i]);
 #pragma unroll
@@ -73,9 +73,9 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
             for (int e = 0; e < 8; ++e) qf[i][e] = 0.0f;
         }
     }
-    float m[kMaxGroup], l[kMaxGroup], o[kMaxGroup][8];
+    float m[G], l[G], o[G][8];
 #pragma unroll
-    for (int i = 0; i < kMaxGroup; ++i) {
+    for (int i = 0; i < G; ++i) {
         m[i] = -INFINITY;
         l[i] = 0.0f;
 #pragma unroll
@@ -89,39 +89,49 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     const uint64_t row_pitch = (uint64_t)Hkv * Dh;
     const T* kbase = kc + (uint64_t)b * max_len * row_pitch + (uint64_t)g * Dh + d0;
     const T* vbase = vc + (uint64_t)b * max_len * row_pitch + (uint64_t)g * Dh + d0;
-    for (uint32_t p0 = pbeg + warp * KPW; p0 < pend; p0 += NW * KPW) {
-        const uint32_t pos = p0 + grp;
-        const bool valid = pos < pend;
-        float kf[8], vf[8];
-        if (valid && dvalid) {
-            unpack8<T>(*reinterpret_cast<const Vec8*>(kbase + (uint64_t)pos * row_pitch), kf);
-            unpack8<T>(*reinterpret_cast<const Vec8*>(vbase + (uint64_t)pos * row_pitch), vf);
-        } else {
+    // Each lane group loads U cached rows (K and V, 16 bytes per lane each)
+    // before consuming them, so 2*U loads per lane are in flight.
+    constexpr int U = 4;
+    for (uint32_t p0 = pbeg + warp * KPW * U; p0 < pend; p0 += NW * KPW * U) {
+        float kf[U][8], vf[U][8];
+        bool valid[U];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) kf[e] = vf[e] = 0.0f;
+        for (int u = 0; u < U; ++u) {
+            const uint32_t pos = p0 + u * KPW + grp;
+            valid[u] = pos < pend;
+            if (valid[u] && dvalid) {
+                unpack8<T>(*reinterpret_cast<const Vec8*>(kbase + (uint64_t)pos * row_pitch), kf[u]);
+                unpack8<T>(*reinterpret_cast<const Vec8*>(vbase + (uint64_t)pos * row_pitch), vf[u]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) kf[u][e] = vf[u][e] = 0.0f;
+            }
         }
 #pragma unroll
-        for (int i = 0; i < kMaxGroup; ++i) {
-            if (i >= (int)nh) break;
-            float s = 0.0f;
+        for (int u = 0; u < U; ++u) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) s = fmaf(qf[i][e], kf[e], s);
+            for (int i = 0; i < G; ++i) {
+                if (i >= (int)nh) break;
+                float sdot = 0.0f;
 #pragma unroll
-            for (int off = LPK / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-            if (valid) {
-                float mn = fmaxf(m[i], s);
-                float a = ex2f(m[i] - mn);
-                float p = ex2f(s - mn);
-                l[i] = l[i] * a + p;
+                for (int e = 0; e < 8; ++e) sdot = fmaf(qf[i][e], kf[u][e], sdot);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) o[i][e] = fmaf(o[i][e], a, p * vf[e]);
-                m[i] = mn;
+                for (int off = LPK / 2; off > 0; off >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, off);
+                if (valid[u]) {
+                    const float mn = fmaxf(m[i], sdot);
+                    const float a = ex2f(m[i] - mn);
+                    const float p = ex2f(sdot - mn);
+                    l[i] = l[i] * a + p;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o[i][e] = fmaf(o[i][e], a, p * vf[u][e]);
+                    m[i] = mn;
+                }
             }
         }
     }
     // Merge the KPW row groups of the warp (lanes with equal `sub`).
 #pragma unroll
-    for (int i = 0; i < kMaxGroup; ++i) {
+    for (int i = 0; i < G; ++i) {
         if (i >= (int)nh) break;
 #pragma unroll
         for (int off = LPK; off < 32; off <<= 1) {
@@ -205,10 +215,10 @@ int launch_decode(const void* q, const void* k, const void* v, void* o, uint32_t
                   cudaStream_t st) {
     DeviceState* ds = state();
     const uint32_t Gq = H / Hkv;
-    const uint32_t hgroups = (Gq + kMaxGroup - 1) / kMaxGroup;
+    const uint32_t hgroups = (Gq + kMaxGroup - 1) / kMaxGroup;  // same grouping for G = 1 (Gq = 1)
     const uint64_t ctas_wo_split = (uint64_t)B * Hkv * hgroups;
-    // Split positions so that the grid covers ~2 waves, at least 64 rows each.
-    uint64_t want = std::max<uint64_t>(1, (2ull * ds->sm_count + ctas_wo_split - 1) / ctas_wo_split);
+    // Split positions so that the grid covers ~4 CTAs per SM, at least 64 rows each.
+    uint64_t want = std::max<uint64_t>(1, (4ull * ds->sm_count + ctas_wo_split - 1) / ctas_wo_split);
     uint32_t chunk = (uint32_t)std::max<uint64_t>(64, (cur_len + want - 1) / want);
     chunk = (chunk + 31) / 32 * 32;
     const uint32_t nsplit = (cur_len + chunk - 1) / chunk;
@@ -218,10 +228,15 @@ int launch_decode(const void* q, const void* k, const void* v, void* o, uint32_t
     char* ws = (char*)workspace(WS_DECODE, toff + pbytes);
     if (!ws) return fail(EVKCU_CUDA_ERROR, "evkcu_single_query_attention: scratch allocation failed");
     dim3 grid(nsplit, Hkv * hgroups, B);
-    decode_attn_kernel<T, LPK><<<grid, kDecThreads, 0, st>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, H, Hkv, Dh,
-                                                            max_len, cur_len, d_cur_len, chunk, scale_log2,
-                                                            (float*)(ws + toff),
-                                                            (unsigned int*)ws);
+    // MHA (one query head per cached head) needs no head group registers.
+    if (Gq == 1)
+        decode_attn_kernel<T, LPK, 1><<<grid, kDecThreads, 0, st>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, H,
+                                                                   Hkv, Dh, max_len, cur_len, d_cur_len, chunk,
+                                                                   scale_log2, (float*)(ws + toff), (unsigned int*)ws);
+    else
+        decode_attn_kernel<T, LPK, kMaxGroup><<<grid, kDecThreads, 0, st>>>(
+            (const T*)q, (const T*)k, (const T*)v, (T*)o, H, Hkv, Dh, max_len, cur_len, d_cur_len, chunk, scale_log2,
+            (float*)(ws + toff), (unsigned int*)ws);
     return after_launch("evkcu_single_query_attention");
 }
 

@@ -183,23 +183,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 // --------------------------------------------------------- small-M GEMV ----
 // y[m, n] = sum_k x[m, k] * W[k, n]          (W row-major [K, N], !transpose_b)
-// One CTA = 8 warps over a 256-column slab; warp w takes k = w, w+8, ... of
-// the CTA's K range, each lane 8 consecutive columns (16-byte loads), x rows
-// staged in shared memory.  K is split over gridDim.y CTAs; their fp32
-// partials are combined by the last CTA of each slab (atomic ticket).
+// The weight stream is the roofline, so the kernel keeps many 16-byte loads
+// in flight: one CTA covers a 64-column slab and a K range; lane l of warp w
+// owns columns 8*(l % 8) .. +7 and k-group w*4 + l/8 (32 k-groups), and
+// issues 4 rows' loads (rows kg, kg+32, kg+64, kg+96) before using them.  x
+// rows are staged in shared memory.  K is split over gridDim.y CTAs, sized
+// for ~4 CTAs per SM; the last CTA of each slab (atomic ticket) adds the fp32
+// partials.
 constexpr int kGemvMaxM = 16;
-constexpr int kGemvKChunk = 256;  // k rows staged per shared-memory fill
+constexpr int kGemvSlab = 64;
+constexpr int kGemvKGroups = 32;
+constexpr int kGemvXChunk = 256;  // x columns staged per shared-memory fill
+constexpr int kGemvUnroll = 4;
 
 template <typename T, int MM>
 __global__ void __launch_bounds__(256) gemv_nn_kernel(const T* __restrict__ X, const T* __restrict__ W,
                                                       T* __restrict__ Y, uint32_t Mt, uint32_t K, uint32_t N,
                                                       uint32_t k_per_cta, int acc_c, float* __restrict__ partial,
                                                       unsigned int* __restrict__ tickets) {
-    __shared__ float xs[MM][kGemvKChunk];
-    __shared__ float red[MM][256];  // per-slab sums over the 8 warps (shared atomics)
+    __shared__ float xs[MM][kGemvXChunk];
+    __shared__ float red[MM][kGemvSlab];
     __shared__ bool is_last;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t col = blockIdx.x * 256 + lane * 8;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cg = lane & 7;
+    const int kg = warp * 4 + (lane >> 3);
+    const uint32_t col = blockIdx.x * kGemvSlab + cg * 8;
+    const bool cvalid = col < N;
     const uint32_t kbeg = blockIdx.y * k_per_cta;
     const uint32_t kend = min(kbeg + k_per_cta, K);
     float acc[MM][8];
@@ -207,41 +216,65 @@ __global__ void __launch_bounds__(256) gemv_nn_kernel(const T* __restrict__ X, c
     for (int m = 0; m < MM; ++m)
 #pragma unroll
         for (int e = 0; e < 8; ++e) acc[m][e] = 0.0f;
-    for (uint32_t i = threadIdx.x; i < MM * 256; i += blockDim.x) red[i / 256][i % 256] = 0.0f;
+    for (uint32_t i = threadIdx.x; i < MM * kGemvSlab; i += blockDim.x) red[i / kGemvSlab][i % kGemvSlab] = 0.0f;
 
-    for (uint32_t kc = kbeg; kc < kend; kc += kGemvKChunk) {
-        const uint32_t kn = min((uint32_t)kGemvKChunk, kend - kc);
+    for (uint32_t kc = kbeg; kc < kend; kc += kGemvXChunk) {
+        const uint32_t kn = min((uint32_t)kGemvXChunk, kend - kc);
         __syncthreads();
-        for (uint32_t i = threadIdx.x; i < MM * kGemvKChunk; i += blockDim.x) {
-            uint32_t m = i / kGemvKChunk, kk = i % kGemvKChunk;
+        for (uint32_t i = threadIdx.x; i < MM * kGemvXChunk; i += blockDim.x) {
+            const uint32_t m = i / kGemvXChunk, kk = i % kGemvXChunk;
             xs[m][kk] = (kk < kn && m < Mt) ? Elem<T>::to_f(X[(uint64_t)m * K + kc + kk]) : 0.0f;
         }
         __syncthreads();
-        if (col < N) {
-#pragma unroll 4
-            for (uint32_t kk = warp; kk < kn; kk += 8) {
-                float w[8];
-                unpack8<T>(*reinterpret_cast<const Vec8*>(W + (uint64_t)(kc + kk) * N + col), w);
+        if (!cvalid) continue;
+        for (uint32_t k0 = kg; k0 < kn; k0 += kGemvKGroups * kGemvUnroll) {
+            Vec8 w[kGemvUnroll];
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; ++u) {
+                const uint32_t kk = k0 + u * kGemvKGroups;
+                if (kk < kn) w[u] = *reinterpret_cast<const Vec8*>(W + (uint64_t)(kc + kk) * N + col);
+                else w[u] = Vec8{{0u, 0u, 0u, 0u}};
+            }
+#pragma unroll
+            for (int u = 0; u < kGemvUnroll; ++u) {
+                const uint32_t kk = min(k0 + u * kGemvKGroups, (uint32_t)kGemvXChunk - 1);
+                float wf[8];
+                unpack8<T>(w[u], wf);
 #pragma unroll
                 for (int m = 0; m < MM; ++m) {
-                    float xv = xs[m][kk];
+                    const float xv = xs[m][kk];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) acc[m][e] = fmaf(xv, w[e], acc[m][e]);
+                    for (int e = 0; e < 8; ++e) acc[m][e] = fmaf(xv, wf[e], acc[m][e]);
                 }
             }
         }
     }
-    __syncthreads();
+    // Sum the 4 k-groups of each warp that share a column group, then the 8 warps.
 #pragma unroll
     for (int m = 0; m < MM; ++m)
-        if (m < (int)Mt)
 #pragma unroll
-            for (int e = 0; e < 8; ++e) atomicAdd(&red[m][lane * 8 + e], acc[m][e]);
+        for (int e = 0; e < 8; ++e) {
+            float v = acc[m][e];
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            acc[m][e] = v;
+        }
+    // Warps add in a fixed order so results are bit-reproducible.
+    for (int w = 0; w < 8; ++w) {
+        __syncthreads();
+        if (warp == w && lane < 8) {
+#pragma unroll
+            for (int m = 0; m < MM; ++m)
+                if (m < (int)Mt)
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) red[m][cg * 8 + e] += acc[m][e];
+        }
+    }
     __syncthreads();
-    const uint32_t n_out = Mt * 256;
+    const uint32_t n_out = Mt * kGemvSlab;
     if (gridDim.y == 1) {
         for (uint32_t i = threadIdx.x; i < n_out; i += blockDim.x) {
-            uint32_t m = i / 256, c = i % 256, n = blockIdx.x * 256 + c;
+            const uint32_t m = i / kGemvSlab, c = i % kGemvSlab, n = blockIdx.x * kGemvSlab + c;
             if (n < N) {
                 float v = red[m][c];
                 if (acc_c) v += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
@@ -252,7 +285,7 @@ __global__ void __launch_bounds__(256) gemv_nn_kernel(const T* __restrict__ X, c
     }
     // Split-K: publish this CTA's partial, the last CTA of the slab reduces.
     float* my = partial + ((uint64_t)blockIdx.x * gridDim.y + blockIdx.y) * n_out;
-    for (uint32_t i = threadIdx.x; i < n_out; i += blockDim.x) my[i] = red[i / 256][i % 256];
+    for (uint32_t i = threadIdx.x; i < n_out; i += blockDim.x) my[i] = red[i / kGemvSlab][i % kGemvSlab];
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) is_last = atomicAdd(&tickets[blockIdx.x], 1u) == gridDim.y - 1;
@@ -261,12 +294,12 @@ __global__ void __launch_bounds__(256) gemv_nn_kernel(const T* __restrict__ X, c
     __threadfence();
     const float* base = partial + (uint64_t)blockIdx.x * gridDim.y * n_out;
     for (uint32_t i = threadIdx.x; i < n_out; i += blockDim.x) {
-        uint32_t m = i / 256, c = i % 256, n = blockIdx.x * 256 + c;
-        float s = 0.0f;
-        for (uint32_t y = 0; y < gridDim.y; ++y) s += ((volatile const float*)base)[(uint64_t)y * n_out + i];
+        const uint32_t m = i / kGemvSlab, c = i % kGemvSlab, n = blockIdx.x * kGemvSlab + c;
+        float sum = 0.0f;
+        for (uint32_t y = 0; y < gridDim.y; ++y) sum += ((volatile const float*)base)[(uint64_t)y * n_out + i];
         if (n < N) {
-            if (acc_c) s += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
-            Y[(uint64_t)m * N + n] = Elem<T>::from_f(s);
+            if (acc_c) sum += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
+            Y[(uint64_t)m * N + n] = Elem<T>::from_f(sum);
         }
     }
     if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
@@ -349,31 +382,35 @@ int launch_gemv(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t 
         }
         return after_launch("evkcu_matmul(gemv_nt)");
     }
-    uint32_t slabs = (N + 255) / 256;
-    // Split K so that slabs * splits covers ~2 waves of SMs, 256-row granules.
-    uint32_t want = std::max<uint32_t>(1, (uint32_t)(2 * s->sm_count) / std::max<uint32_t>(1, slabs));
-    uint32_t max_split = std::max<uint32_t>(1, (K + kGemvKChunk - 1) / kGemvKChunk);
+    const uint32_t slabs = (N + kGemvSlab - 1) / kGemvSlab;
+    // Split K so that slabs * splits covers ~4 CTAs per SM, >= 128 rows each.
+    const uint32_t want = std::max<uint32_t>(1, (uint32_t)(4 * s->sm_count + slabs - 1) / slabs);
+    const uint32_t max_split = std::max<uint32_t>(1, K / 128);
     uint32_t splits = std::min(want, max_split);
-    uint32_t k_per = ((K + splits - 1) / splits + 7) / 8 * 8;
+    const uint32_t k_per = ((K + splits - 1) / splits + kGemvKGroups - 1) / kGemvKGroups * kGemvKGroups;
     splits = (K + k_per - 1) / k_per;
     float* partial = nullptr;
     unsigned int* tickets = nullptr;
     if (splits > 1) {
-        size_t pbytes = (size_t)slabs * splits * Mt * 256 * sizeof(float);
         if (slabs > kMaxTickets) return fail(EVKCU_BAD_SHAPE, "evkcu_matmul: N too large for the GEMV path");
-        const size_t tbytes = kTicketBytes;
-        char* ws = (char*)workspace(WS_GEMV, pbytes + tbytes);
+        const size_t pbytes = (size_t)slabs * splits * Mt * kGemvSlab * sizeof(float);
+        char* ws = (char*)workspace(WS_GEMV, kTicketBytes + pbytes);
         if (!ws) return fail(EVKCU_CUDA_ERROR, "evkcu_matmul: workspace allocation failed");
         tickets = (unsigned int*)ws;
-        partial = (float*)(ws + tbytes);
+        partial = (float*)(ws + kTicketBytes);
     }
     dim3 grid(slabs, splits);
     // Tickets start at zero (zero-filled scratch); the reducing CTA resets its entry.
-    switch ((Mt + 3) / 4) {
-        case 1: gemv_nn_kernel<T, 4><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets); break;
-        case 2: gemv_nn_kernel<T, 8><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets); break;
-        default: gemv_nn_kernel<T, 16><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets); break;
-    }
+    if (Mt <= 1)
+        gemv_nn_kernel<T, 1><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets);
+    else if (Mt <= 2)
+        gemv_nn_kernel<T, 2><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets);
+    else if (Mt <= 4)
+        gemv_nn_kernel<T, 4><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets);
+    else if (Mt <= 8)
+        gemv_nn_kernel<T, 8><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets);
+    else
+        gemv_nn_kernel<T, 16><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets);
     return after_launch("evkcu_matmul(gemv_nn)");
 }
 
