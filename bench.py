@@ -187,6 +187,69 @@ def gemm_leg(torch, evk, dtype, n=8192, reps=20):
     return 2.0 * n ** 3 / (ms * 1e-3) / 1e12
 
 
+# LLM configurations of BASELINE.json (random weights, synthetic prompts):
+# name -> (layers, d_model, heads, hidden, vocab, batch, prompt, decode steps, dtype, tied)
+LLM_CONFIGS = {
+    "C3_tiny": (6, 512, 8, 2048, 32000, 1, 128, 256, 0, True),
+    "C4_1.3B": (24, 2048, 16, 8192, 32000, 8, 2048, 64, 1, False),
+    "C5_8B_shape": (32, 4096, 32, 14336, 128256, 16, 4096, 16, 1, False),
+}
+
+
+def llm_leg(torch, evk, name, comm=None, rank=0, world=1):
+    """Prefill TFLOP/s and decode tok/s of one LLM config through the C ABI
+    (evkcu_llm_*), tensor-parallel over `world` GPUs.  Device-timed with CUDA
+    events; decode steps replay the captured CUDA graph.  FLOPs count the
+    projection GEMMs (2 * params * tokens), causal attention and the LM head."""
+    L, D, H, F, V, B, S, steps, dt, tied = LLM_CONFIGS[name]
+    if world > 1 and (H % world or V % world):
+        return None
+    m = evk.Llm(L, D, H, F, V, B, S + steps + 8, dtype=dt, tied_embeddings=tied, tp_rank=rank, tp_size=world,
+                comm=comm)
+    m.init_random(42, 0.02)
+    st = torch.cuda.Stream()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    tok = torch.randint(0, V, (B, S), dtype=torch.int32, device="cuda", generator=g)
+    nxt = torch.zeros(B, dtype=torch.int32, device="cuda")
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        m.prefill(tok, nxt, stream=st)
+        st.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        ev0.record(st)
+        m.prefill(tok, nxt, stream=st)
+        ev1.record(st)
+        st.synchronize()
+        pf_ms = ev0.elapsed_time(ev1)
+        bufs = [torch.zeros(B, dtype=torch.int32, device="cuda") for _ in range(2)]
+        cur = nxt.clone()
+        warm = 3
+        for i in range(warm):
+            m.decode(cur, bufs[i % 2], stream=st)
+            cur = bufs[i % 2]
+        st.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        ev0.record(st)
+        for i in range(steps - warm):
+            m.decode(cur, bufs[i % 2], stream=st)
+            cur = bufs[i % 2]
+        ev1.record(st)
+        st.synchronize()
+        dec_ms = ev0.elapsed_time(ev1) / (steps - warm)
+    m.close()
+    if world > 1:
+        t = torch.tensor([pf_ms, dec_ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        pf_ms, dec_ms = t.tolist()
+    params = L * (4 * D * D + 2 * D * F) + (0 if tied else D * V)
+    flops = 2.0 * params * B * S + L * 4.0 * B * S * S * D / 2 + 2.0 * D * V * B
+    return {"prefill_ms": round(pf_ms, 2), "prefill_tflops": round(flops / pf_ms / 1e9, 1),
+            "decode_ms_per_step": round(dec_ms, 3), "decode_tok_s": round(B / dec_ms * 1e3, 1),
+            "batch": B, "prompt": S, "tp": world}
+
+
 def profile_leg(leg):
     """A few launches of one leg on resident inputs: the small case ncu captures."""
     import torch
@@ -320,6 +383,19 @@ def main():
     if not args.no_extra:
         extra["gemm_8192_bf16_tflops"] = round(gemm_leg(torch, evk, torch.bfloat16), 1)
         extra["gemm_8192_f16_tflops"] = round(gemm_leg(torch, evk, torch.float16), 1)
+        comm = None
+        if ws > 1:
+            uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+            if rank == 0:
+                uid.copy_(torch.frombuffer(bytearray(evk.Comm.unique_id()), dtype=torch.uint8))
+            torch.distributed.broadcast(uid, 0)
+            comm = evk.Comm(bytes(uid.cpu().numpy()), rank, ws)
+        llm = {}
+        for name in (["C3_tiny"] if ws == 1 else []) + ["C4_1.3B", "C5_8B_shape"]:
+            llm[name] = llm_leg(torch, evk, name, comm, rank, ws)
+        extra["llm"] = llm
+        if comm:
+            comm.close()
 
     if ws > 1:
         torch.distributed.barrier()
