@@ -18,11 +18,12 @@
 //    to a batch extent of 1 in the tensor map.  M/N/K tails are handled by
 //    TMA zero fill and epilogue guards.
 //
-//  * small-M path (decode, M*batch <= 16 with a shared B): a CUDA-core GEMV
-//    that streams B once with 16-byte loads — the weight read is the roofline
-//    there, and a 128-row MMA tile would be 8-128x padded.
+//  * small-M path (decode, M*batch <= 16 with a shared B): a transposed
+//    tcgen05 GEMV (see gemv_tc_kernel) that streams B once through TMA — the
+//    weight read is the roofline there.
 #include <algorithm>
 #include <string>
+#include <type_traits>
 
 #include "sm100.cuh"
 
@@ -182,121 +183,174 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // --------------------------------------------------------- small-M GEMV ----
-// y[m, n] = sum_k x[m, k] * W[k, n]          (W row-major [K, N], !transpose_b)
-// The weight stream is the roofline, so the kernel keeps many 16-byte loads
-// in flight: one CTA covers a 64-column slab and a K range; lane l of warp w
-// owns columns 8*(l % 8) .. +7 and k-group w*4 + l/8 (32 k-groups), and
-// issues 4 rows' loads (rows kg, kg+32, kg+64, kg+96) before using them.  x
-// rows are staged in shared memory.  K is split over gridDim.y CTAs, sized
-// for ~4 CTAs per SM; the last CTA of each slab (atomic ticket) adds the fp32
-// partials.
+// y[m, n] = sum_k x[m, k] * W[k, n]     (W row-major [K, N]; or [N, K] with
+// transpose_b, e.g. a tied-embedding LM head), for Mt <= 16 rows of x.
+// The weight read is the roofline (2 bytes per weight, each used Mt times),
+// and at Mt = 8..16 even the FMAs would outrun the CUDA cores at full HBM
+// rate, so the product runs on the tensor cores transposed:
+//     y^T[n, m] = sum_k W^T[n, k] * x^T[k, m]
+// One CTA owns a 128-column slab of W (the MMA's M = 128) and a range of
+// 64-deep k-tiles.  W is the A operand (MN-major for row-major W, K-major for
+// transpose_b), x is the B operand (K-major, N = 16 rows, rows >= Mt
+// zero-filled by TMA).  Warp 0 streams W/x k-tiles through a GV_STAGES-deep
+// ring, warp 1 issues tcgen05.mma into a 128 x 16 fp32 TMEM accumulator,
+// warps 2-5 read it back (TMEM lane = output column).  The grid is one
+// resident wave (two CTAs per SM); K is split across gridDim.y CTAs whose
+// fp32 partials the last CTA of each slab (atomic ticket) adds in split order,
+// so results are bit-reproducible.
 constexpr int kGemvMaxM = 16;
-constexpr int kGemvSlab = 64;
-constexpr int kGemvKGroups = 32;
-constexpr int kGemvXChunk = 256;  // x columns staged per shared-memory fill
-constexpr int kGemvUnroll = 4;
+constexpr int GV_COLS = 128;
+constexpr int GV_BK = 64;
+constexpr int GV_MMA_N = 16;
+constexpr int GV_STAGES = 6;
+constexpr int GV_W_BYTES = GV_COLS * GV_BK * 2;    // 16 KB
+constexpr int GV_X_BYTES = GV_MMA_N * GV_BK * 2;   // 2 KB
+constexpr int GV_STAGE_BYTES = GV_W_BYTES + GV_X_BYTES;
+constexpr int GV_SMEM = GV_STAGES * GV_STAGE_BYTES + 1024 + 256;
+constexpr int GV_THREADS = 192;
+constexpr uint32_t kTimeoutGemv = 0x301;
 
-template <typename T, int MM>
-__global__ void __launch_bounds__(256) gemv_nn_kernel(const T* __restrict__ X, const T* __restrict__ W,
-                                                      T* __restrict__ Y, uint32_t Mt, uint32_t K, uint32_t N,
-                                                      uint32_t k_per_cta, int acc_c, float* __restrict__ partial,
-                                                      unsigned int* __restrict__ tickets) {
-    __shared__ float xs[MM][kGemvXChunk];
-    __shared__ float red[MM][kGemvSlab];
+template <typename T, bool W_KMAJOR>
+__global__ void __launch_bounds__(GV_THREADS, 2)
+    gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                   T* __restrict__ Y, uint32_t Mt, uint32_t K, uint32_t N, uint32_t ktiles_per_cta, int acc_c,
+                   uint32_t idesc, float* __restrict__ partial, unsigned int* __restrict__ tickets,
+                   unsigned int* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sW = smem;
+    uint8_t* sX = smem + GV_STAGES * GV_W_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + GV_STAGES * GV_STAGE_BYTES);
+    uint64_t* empty = full + GV_STAGES;
+    uint64_t* accum = empty + GV_STAGES;
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accum + 1);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
     __shared__ bool is_last;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int cg = lane & 7;
-    const int kg = warp * 4 + (lane >> 3);
-    const uint32_t col = blockIdx.x * kGemvSlab + cg * 8;
-    const bool cvalid = col < N;
-    const uint32_t kbeg = blockIdx.y * k_per_cta;
-    const uint32_t kend = min(kbeg + k_per_cta, K);
-    float acc[MM][8];
-#pragma unroll
-    for (int m = 0; m < MM; ++m)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[m][e] = 0.0f;
-    for (uint32_t i = threadIdx.x; i < MM * kGemvSlab; i += blockDim.x) red[i / kGemvSlab][i % kGemvSlab] = 0.0f;
 
-    for (uint32_t kc = kbeg; kc < kend; kc += kGemvXChunk) {
-        const uint32_t kn = min((uint32_t)kGemvXChunk, kend - kc);
-        __syncthreads();
-        for (uint32_t i = threadIdx.x; i < MM * kGemvXChunk; i += blockDim.x) {
-            const uint32_t m = i / kGemvXChunk, kk = i % kGemvXChunk;
-            xs[m][kk] = (kk < kn && m < Mt) ? Elem<T>::to_f(X[(uint64_t)m * K + kc + kk]) : 0.0f;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t n0 = blockIdx.x * GV_COLS;
+    const uint32_t kt_total = (K + GV_BK - 1) / GV_BK;
+    const uint32_t kt0 = blockIdx.y * ktiles_per_cta;
+    const uint32_t kt1 = min(kt0 + ktiles_per_cta, kt_total);
+    const uint32_t nkt = kt1 > kt0 ? kt1 - kt0 : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < GV_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
         }
-        __syncthreads();
-        if (!cvalid) continue;
-        for (uint32_t k0 = kg; k0 < kn; k0 += kGemvKGroups * kGemvUnroll) {
-            Vec8 w[kGemvUnroll];
-#pragma unroll
-            for (int u = 0; u < kGemvUnroll; ++u) {
-                const uint32_t kk = k0 + u * kGemvKGroups;
-                if (kk < kn) w[u] = *reinterpret_cast<const Vec8*>(W + (uint64_t)(kc + kk) * N + col);
-                else w[u] = Vec8{{0u, 0u, 0u, 0u}};
+        mbar_init(accum, 1);
+        *s_abort = 0;
+        fence_barrier_init();
+        prefetch_tmap(&tmW);
+        prefetch_tmap(&tmX);
+    }
+    if (warp == 1) {
+        tmem_alloc(s_tmem, 32);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            for (uint32_t i = 0; i < nkt; ++i) {
+                const int s = i % GV_STAGES;
+                if (!mbar_wait(&empty[s], ((i / GV_STAGES) & 1) ^ 1, s_abort, err, kTimeoutGemv)) break;
+                mbar_arrive_expect_tx(&full[s], GV_STAGE_BYTES);
+                const int k0 = (int)((kt0 + i) * GV_BK);
+                uint8_t* w = sW + s * GV_W_BYTES;
+                if (W_KMAJOR) {
+                    tma_load_3d(w, &tmW, &full[s], k0, (int)n0, 0);
+                } else {
+                    tma_load_3d(w, &tmW, &full[s], (int)n0, k0, 0);
+                    tma_load_3d(w + GV_W_BYTES / 2, &tmW, &full[s], (int)n0 + 64, k0, 0);
+                }
+                tma_load_3d(sX + s * GV_X_BYTES, &tmX, &full[s], k0, 0, 0);
             }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool ok = true;
+            for (uint32_t i = 0; i < nkt; ++i) {
+                const int s = i % GV_STAGES;
+                if (!mbar_wait(&full[s], (i / GV_STAGES) & 1, s_abort, err, kTimeoutGemv)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = smem_u32(sW + s * GV_W_BYTES);
+                const uint32_t b = smem_u32(sX + s * GV_X_BYTES);
 #pragma unroll
-            for (int u = 0; u < kGemvUnroll; ++u) {
-                const uint32_t kk = min(k0 + u * kGemvKGroups, (uint32_t)kGemvXChunk - 1);
-                float wf[8];
-                unpack8<T>(w[u], wf);
+                for (int k = 0; k < GV_BK / 16; ++k) {
+                    const uint64_t ad =
+                        W_KMAJOR ? make_sw128_desc(a + k * 32, 16, 1024) : make_sw128_desc(a + k * 2048, 8192, 1024);
+                    const uint64_t bd = make_sw128_desc(b + k * 32, 16, 1024);
+                    mma_f16_ss(tmem, ad, bd, idesc, (i | k) != 0);
+                }
+                mma_commit(&empty[s]);
+            }
+            if (ok) mma_commit(accum);
+        }
+    }
+    // Warps 2-5: TMEM lane quarter q = warp % 4 holds output columns
+    // n0 + 32q .. +31, one per lane, with the Mt rows of x in columns 0..15.
+    float v[GV_MMA_N];
+    bool have = false;
+    const int q = warp & 3;
+    const uint32_t nn = q * 32 + lane;
+    if (warp >= 2) {
+        have = nkt == 0 || mbar_wait(accum, 0, s_abort, err, kTimeoutGemv);
+        tc_fence_after();
+        if (nkt == 0) {
 #pragma unroll
-                for (int m = 0; m < MM; ++m) {
-                    const float xv = xs[m][kk];
+            for (int m = 0; m < GV_MMA_N; ++m) v[m] = 0.0f;
+        } else if (have) {
+            uint32_t r[16];
+            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16), r);
+            tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) acc[m][e] = fmaf(xv, wf[e], acc[m][e]);
+            for (int m = 0; m < GV_MMA_N; ++m) v[m] = __uint_as_float(r[m]);
+        }
+        tc_fence_before();
+        if (have && gridDim.y == 1) {
+            const uint32_t n = n0 + nn;
+            if (n < N) {
+#pragma unroll
+                for (int m = 0; m < GV_MMA_N; ++m) {
+                    if (m < (int)Mt) {
+                        float o = v[m];
+                        if (acc_c) o += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
+                        Y[(uint64_t)m * N + n] = Elem<T>::from_f(o);
+                    }
                 }
             }
-        }
-    }
-    // Sum the 4 k-groups of each warp that share a column group, then the 8 warps.
+        } else if (have) {
+            float* my = partial + ((uint64_t)blockIdx.x * gridDim.y + blockIdx.y) * (GV_MMA_N * GV_COLS);
 #pragma unroll
-    for (int m = 0; m < MM; ++m)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            float v = acc[m][e];
-            v += __shfl_xor_sync(0xffffffffu, v, 8);
-            v += __shfl_xor_sync(0xffffffffu, v, 16);
-            acc[m][e] = v;
-        }
-    // Warps add in a fixed order so results are bit-reproducible.
-    for (int w = 0; w < 8; ++w) {
-        __syncthreads();
-        if (warp == w && lane < 8) {
-#pragma unroll
-            for (int m = 0; m < MM; ++m)
-                if (m < (int)Mt)
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) red[m][cg * 8 + e] += acc[m][e];
+            for (int m = 0; m < GV_MMA_N; ++m)
+                if (m < (int)Mt) my[m * GV_COLS + nn] = v[m];
+            __threadfence();
         }
     }
     __syncthreads();
-    const uint32_t n_out = Mt * kGemvSlab;
-    if (gridDim.y == 1) {
-        for (uint32_t i = threadIdx.x; i < n_out; i += blockDim.x) {
-            const uint32_t m = i / kGemvSlab, c = i % kGemvSlab, n = blockIdx.x * kGemvSlab + c;
-            if (n < N) {
-                float v = red[m][c];
-                if (acc_c) v += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
-                Y[(uint64_t)m * N + n] = Elem<T>::from_f(v);
-            }
-        }
-        return;
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 32);
     }
-    // Split-K: publish this CTA's partial, the last CTA of the slab reduces.
-    float* my = partial + ((uint64_t)blockIdx.x * gridDim.y + blockIdx.y) * n_out;
-    for (uint32_t i = threadIdx.x; i < n_out; i += blockDim.x) my[i] = red[i / kGemvSlab][i % kGemvSlab];
-    __threadfence();
-    __syncthreads();
+    if (gridDim.y == 1 || *s_abort) return;
     if (threadIdx.x == 0) is_last = atomicAdd(&tickets[blockIdx.x], 1u) == gridDim.y - 1;
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    const float* base = partial + (uint64_t)blockIdx.x * gridDim.y * n_out;
-    for (uint32_t i = threadIdx.x; i < n_out; i += blockDim.x) {
-        const uint32_t m = i / kGemvSlab, c = i % kGemvSlab, n = blockIdx.x * kGemvSlab + c;
+    const float* base = partial + (uint64_t)blockIdx.x * gridDim.y * (GV_MMA_N * GV_COLS);
+    for (uint32_t i = threadIdx.x; i < Mt * GV_COLS; i += blockDim.x) {
+        const uint32_t m = i / GV_COLS, c = i % GV_COLS, n = n0 + c;
         float sum = 0.0f;
-        for (uint32_t y = 0; y < gridDim.y; ++y) sum += ((volatile const float*)base)[(uint64_t)y * n_out + i];
+        for (uint32_t y = 0; y < gridDim.y; ++y)
+            sum += ((volatile const float*)base)[(uint64_t)y * (GV_MMA_N * GV_COLS) + i];
         if (n < N) {
             if (acc_c) sum += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
             Y[(uint64_t)m * N + n] = Elem<T>::from_f(sum);
@@ -305,43 +359,43 @@ __global__ void __launch_bounds__(256) gemv_nn_kernel(const T* __restrict__ X, c
     if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
 }
 
-// y[m, n] = sum_k x[m, k] * W[n, k]          (W row-major [N, K], transpose_b)
-// One warp per output column n (all MM rows), lanes split K with 16-byte
-// loads, warp-shuffle reduction.  Used for tied-embedding LM heads.
-template <typename T, int MM>
-__global__ void __launch_bounds__(256) gemv_nt_kernel(const T* __restrict__ X, const T* __restrict__ W,
-                                                      T* __restrict__ Y, uint32_t Mt, uint32_t K, uint32_t N,
-                                                      int acc_c) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t nwarps = gridDim.x * 8;
-    for (uint32_t n = blockIdx.x * 8 + warp; n < N; n += nwarps) {
-        float acc[MM];
-#pragma unroll
-        for (int m = 0; m < MM; ++m) acc[m] = 0.0f;
-        const T* wrow = W + (uint64_t)n * K;
-        for (uint32_t k = lane * 8; k < K; k += 256) {
-            float w[8];
-            unpack8<T>(*reinterpret_cast<const Vec8*>(wrow + k), w);
-#pragma unroll
-            for (int m = 0; m < MM; ++m) {
-                if (m >= (int)Mt) break;
-                float x[8];
-                unpack8<T>(*reinterpret_cast<const Vec8*>(X + (uint64_t)m * K + k), x);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) acc[m] = fmaf(x[e], w[e], acc[m]);
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < MM; ++m) {
-            float v = acc[m];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0 && m < (int)Mt) {
-                if (acc_c) v += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
-                Y[(uint64_t)m * N + n] = Elem<T>::from_f(v);
-            }
-        }
+template <typename T, bool W_KMAJOR>
+int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, int acc, int dtype,
+                   cudaStream_t st) {
+    DeviceState* s = state();
+    const uint32_t slabs = (N + GV_COLS - 1) / GV_COLS;
+    const uint32_t ktiles = (K + GV_BK - 1) / GV_BK;
+    // One resident wave: two CTAs per SM, whole k-tiles per split.
+    const uint32_t slots = 2 * (uint32_t)s->sm_count;
+    uint32_t splits = std::max<uint32_t>(1, std::min<uint32_t>(ktiles, slots / slabs));
+    const uint32_t per = (ktiles + splits - 1) / splits;
+    splits = (ktiles + per - 1) / per;
+    CUtensorMap mW, mX;
+    int r = W_KMAJOR ? make_tmap_3d(&mW, W, K, N, 1, K, (uint64_t)K * N, GV_BK, GV_COLS, dtype)
+                     : make_tmap_3d(&mW, W, N, K, 1, N, (uint64_t)K * N, 64, GV_BK, dtype);
+    if (r) return r;
+    r = make_tmap_3d(&mX, X, K, Mt, 1, K, (uint64_t)K * Mt, GV_BK, GV_MMA_N, dtype);
+    if (r) return r;
+    float* partial = nullptr;
+    unsigned int* tickets = nullptr;
+    if (splits > 1) {
+        if (slabs > kMaxTickets) return fail(EVKCU_BAD_SHAPE, "evkcu_matmul: N too large for the GEMV path");
+        const size_t pbytes = (size_t)slabs * splits * GV_MMA_N * GV_COLS * sizeof(float);
+        char* ws = (char*)workspace(WS_GEMV, kTicketBytes + pbytes);
+        if (!ws) return fail(EVKCU_CUDA_ERROR, "evkcu_matmul: workspace allocation failed");
+        tickets = (unsigned int*)ws;
+        partial = (float*)(ws + kTicketBytes);
     }
+    auto kern = gemv_tc_kernel<T, W_KMAJOR>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        EVKCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GV_SMEM));
+        attr_set = true;
+    }
+    const uint32_t idesc = make_idesc_f16(GV_COLS, GV_MMA_N, dtype == EVKCU_BF16 ? 1 : 0, W_KMAJOR ? 0 : 1, 0);
+    dim3 grid(slabs, splits);
+    kern<<<grid, GV_THREADS, GV_SMEM, st>>>(mW, mX, Y, Mt, K, N, per, acc, idesc, partial, tickets, s->d_error);
+    return after_launch("evkcu_matmul(gemv_tc)");
 }
 
 template <typename T, int BN, bool A_MN, bool B_MN>
@@ -372,46 +426,9 @@ int dispatch_major(bool ta, bool tb, const CUtensorMap& mA, const CUtensorMap& m
 
 template <typename T>
 int launch_gemv(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, bool tb, int acc, cudaStream_t st) {
-    DeviceState* s = state();
-    if (tb) {
-        unsigned grid = (unsigned)std::min<uint64_t>((N + 7) / 8, (uint64_t)s->sm_count * 8);
-        switch ((Mt + 3) / 4) {
-            case 1: gemv_nt_kernel<T, 4><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, acc); break;
-            case 2: gemv_nt_kernel<T, 8><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, acc); break;
-            default: gemv_nt_kernel<T, 16><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, acc); break;
-        }
-        return after_launch("evkcu_matmul(gemv_nt)");
-    }
-    const uint32_t slabs = (N + kGemvSlab - 1) / kGemvSlab;
-    // Split K so that slabs * splits covers ~4 CTAs per SM, >= 128 rows each.
-    const uint32_t want = std::max<uint32_t>(1, (uint32_t)(4 * s->sm_count + slabs - 1) / slabs);
-    const uint32_t max_split = std::max<uint32_t>(1, K / 128);
-    uint32_t splits = std::min(want, max_split);
-    const uint32_t k_per = ((K + splits - 1) / splits + kGemvKGroups - 1) / kGemvKGroups * kGemvKGroups;
-    splits = (K + k_per - 1) / k_per;
-    float* partial = nullptr;
-    unsigned int* tickets = nullptr;
-    if (splits > 1) {
-        if (slabs > kMaxTickets) return fail(EVKCU_BAD_SHAPE, "evkcu_matmul: N too large for the GEMV path");
-        const size_t pbytes = (size_t)slabs * splits * Mt * kGemvSlab * sizeof(float);
-        char* ws = (char*)workspace(WS_GEMV, kTicketBytes + pbytes);
-        if (!ws) return fail(EVKCU_CUDA_ERROR, "evkcu_matmul: workspace allocation failed");
-        tickets = (unsigned int*)ws;
-        partial = (float*)(ws + kTicketBytes);
-    }
-    dim3 grid(slabs, splits);
-    // Tickets start at zero (zero-filled scratch); the reducing CTA resets its entry.
-    if (Mt <= 1)
-        gemv_nn_kernel<T, 1><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets);
-    else if (Mt <= 2)
-        gemv_nn_kernel<T, 2><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets);
-    else if (Mt <= 4)
-        gemv_nn_kernel<T, 4><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets);
-    else if (Mt <= 8)
-        gemv_nn_kernel<T, 8><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets);
-    else
-        gemv_nn_kernel<T, 16><<<grid, 256, 0, st>>>(X, W, Y, Mt, K, N, k_per, acc, partial, tickets);
-    return after_launch("evkcu_matmul(gemv_nn)");
+    const int dtype = std::is_same<T, __nv_bfloat16>::value ? EVKCU_BF16 : EVKCU_F16;
+    if (tb) return launch_gemv_tc<T, true>(X, W, Y, Mt, K, N, acc, dtype, st);
+    return launch_gemv_tc<T, false>(X, W, Y, Mt, K, N, acc, dtype, st);
 }
 
 }  // namespace

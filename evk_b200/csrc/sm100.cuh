@@ -53,10 +53,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     const uint32_t a = smem_u32(bar);
     if (mbar_try_wait(a, parity)) return true;
     long long t0 = clock64();
-    while (true) {
+    for (uint32_t spin = 1;; ++spin) {
         if (mbar_try_wait(a, parity)) return true;
         if (*abort) return false;
-        // Another CTA already gave up: stop waiting on work that may never come.
+        // Another CTA already gave up: stop waiting on work that may never
+        // come.  The flag is global memory shared by every CTA, so it is polled
+        // only every 256 tries: with whole CTAs waiting, polling it each try
+        // turns one L2 line into a hot spot that slows the data being waited for.
+        if ((spin & 255u) != 0) continue;
         if (err && *reinterpret_cast<volatile unsigned int*>(err)) {
             *abort = 1;
             return false;
