@@ -7,26 +7,36 @@
 // positions, fp32 arithmetic, scale 1/sqrt(Dh) by default, 0 when the weight
 // sum is 0.
 //
-// Here, split-KV flash-decode: grid (splits, Hkv * head_groups, B).  A CTA
-// takes one KV head g, up to 8 of the query heads that read it (GQA/MQA read
-// the cache once for all of them) and one contiguous range of positions.
-// LPK lanes cooperate on one cached row (16 bytes each, so a row is read as
-// whole 32-byte sectors); each lane group keeps its own online-softmax state
-// for its rows; groups and warps merge through shuffles and shared memory;
-// per-split partials (m, l, o[Dh]) go to scratch and the last CTA of each
-// (b, g, head group) merges the splits and writes the output.  The roofline is
-// the KV-cache read: B * cur_len * Hkv * Dh * 2 bytes * 2 (K and V).
+// Here, split-KV flash-decode: grid (splits, Hkv * head_groups, B), one
+// resident wave.  A CTA takes one KV head g, up to 8 of the query heads that
+// read it (GQA/MQA read the cache once for all of them) and one contiguous
+// range of positions.  A producer warp streams the range through a
+// shared-memory ring as ROWS-position K and V tiles (TMA boxes of Dh x ROWS
+// out of the [B * max_len, Hkv * Dh] cache, full/empty mbarriers); eight
+// compute warps read them from shared memory.  LPK lanes cooperate on one
+// row (16 bytes each); each lane group keeps its own online-softmax state and
+// folds in STEPS rows per tile with one rescale; groups and warps merge
+// through shuffles and shared memory; per-split partials (m, l, o[Dh]) go to
+// scratch and the last CTA of each (b, g, head group) merges the splits in
+// split order and writes the output.  The roofline is the KV-cache read:
+// B * cur_len * Hkv * Dh * 2 bytes * 2 (K and V).
 #include <float.h>
 
 #include <algorithm>
 
-#include "common.cuh"
+#include "sm100.cuh"
 
 namespace evkcu {
 namespace {
 
-constexpr int kDecThreads = 128;
-constexpr int kMaxGroup = 8;  // query heads per CTA
+using namespace sm100;
+
+constexpr int kDecCompute = 8;                    // compute warps
+constexpr int kDecThreads = (kDecCompute + 1) * 32;  // + the producer warp
+constexpr int kMaxGroup = 8;                      // query heads per CTA
+constexpr int kMaxStages = 8;
+constexpr uint32_t kDecSmemTarget = 96 * 1024;    // ring bytes: two CTAs per SM
+constexpr uint32_t kTimeoutDecode = 0x401;
 
 __device__ __forceinline__ float ex2f(float x) {
     float y;
@@ -34,22 +44,35 @@ __device__ __forceinline__ float ex2f(float x) {
     return y;
 }
 
+// Tile geometry for LPK lanes per cached row.
+template <int LPK>
+struct DecTile {
+    static constexpr int KPW = 32 / LPK;                                   // rows per warp step
+    static constexpr int ROWS = KPW * kDecCompute > 64 ? KPW * kDecCompute : 64;  // positions per tile
+    static constexpr int STEPS = ROWS / (KPW * kDecCompute);               // steps per warp per tile
+};
+
 // partial layout per (b, h, split): m, l, o[Dh]  (fp32)
 template <typename T, int LPK, int G>
 __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
-    const T* __restrict__ q, const T* __restrict__ kc, const T* __restrict__ vc, T* __restrict__ out, uint32_t H,
-    uint32_t Hkv, uint32_t Dh, uint32_t max_len, uint32_t cur_len, const uint32_t* __restrict__ d_cur_len,
-    uint32_t chunk, float scale_log2,
-    float* __restrict__ partial, unsigned int* __restrict__ tickets) {
-    constexpr int KPW = 32 / LPK;  // rows per warp iteration
-    constexpr int NW = kDecThreads / 32;
+    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const T* __restrict__ q,
+    T* __restrict__ out, uint32_t H, uint32_t Hkv, uint32_t Dh, uint32_t max_len, uint32_t cur_len,
+    const uint32_t* __restrict__ d_cur_len, uint32_t chunk, float scale_log2, uint32_t stages,
+    float* __restrict__ partial, unsigned int* __restrict__ tickets, unsigned int* err) {
+    constexpr int KPW = DecTile<LPK>::KPW, ROWS = DecTile<LPK>::ROWS, STEPS = DecTile<LPK>::STEPS;
+    constexpr int NW = kDecCompute;
     __shared__ float sm_m[NW][G], sm_l[NW][G];
-    __shared__ float sm_o[NW][G][LPK * 8];
+    __shared__ uint64_t full[kMaxStages], empty[kMaxStages];
+    __shared__ int s_abort_v;
     __shared__ bool is_last;
+    // stages x (K tile, V tile); reused for the warps' o partials at the end.
+    extern __shared__ __align__(128) uint8_t ring[];
+    float (*sm_o)[G][LPK * 8] = reinterpret_cast<float (*)[G][LPK * 8]>(ring);
+    volatile int* s_abort = &s_abort_v;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int sub = lane % LPK;   // which 8-element slice of the row
-    const int grp = lane / LPK;   // which row of the warp iteration
+    const int grp = lane / LPK;   // which row of the warp step
     const uint32_t split = blockIdx.x, nsplit = gridDim.x;
     const uint32_t Gq = H / Hkv;
     const uint32_t hgroups = (Gq + G - 1) / G;
@@ -60,19 +83,25 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     const uint32_t b = blockIdx.z;
     const uint32_t d0 = sub * 8;
     const bool dvalid = d0 < Dh;
+    const uint32_t tile_elems = ROWS * Dh;
 
-    float qf[G][8];
-#pragma unroll
-    for (int i = 0; i < G; ++i) {
-        if (i < (int)nh && dvalid) {
-            unpack8<T>(*reinterpret_cast<const Vec8*>(q + ((uint64_t)b * H + h0 + i) * Dh + d0), qf[i]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) qf[i][e] *= scale_log2;
-        } else {
-#pragma unroll
-            for (int e = 0; e < 8; ++e) qf[i][e] = 0.0f;
+    const uint32_t pbeg = split * chunk;
+    // With d_cur_len the length lives in device memory (the grid was sized for
+    // max_len), so a captured graph can replay with a growing cache.
+    const uint32_t len = d_cur_len ? min(*d_cur_len, max_len) : cur_len;
+    const uint32_t pend = min(pbeg + chunk, len);
+    const uint32_t ntiles = pend > pbeg ? (pend - pbeg + ROWS - 1) / ROWS : 0;
+
+    if (threadIdx.x == 0) {
+        for (uint32_t s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NW);
         }
+        *s_abort = 0;
+        fence_barrier_init();
     }
+    __syncthreads();
+
     float m[G], l[G], o[G][8];
 #pragma unroll
     for (int i = 0; i < G; ++i) {
@@ -81,80 +110,154 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
 #pragma unroll
         for (int e = 0; e < 8; ++e) o[i][e] = 0.0f;
     }
-    const uint32_t pbeg = split * chunk;
-    // With d_cur_len the length lives in device memory (the grid was sized for
-    // max_len), so a captured graph can replay with a growing cache.
-    const uint32_t len = d_cur_len ? min(*d_cur_len, max_len) : cur_len;
-    const uint32_t pend = min(pbeg + chunk, len);
-    const uint64_t row_pitch = (uint64_t)Hkv * Dh;
-    const T* kbase = kc + (uint64_t)b * max_len * row_pitch + (uint64_t)g * Dh + d0;
-    const T* vbase = vc + (uint64_t)b * max_len * row_pitch + (uint64_t)g * Dh + d0;
-    // Each lane group loads U cached rows (K and V, 16 bytes per lane each)
-    // before consuming them, so 2*U loads per lane are in flight.
-    constexpr int U = 4;
-    for (uint32_t p0 = pbeg + warp * KPW * U; p0 < pend; p0 += NW * KPW * U) {
-        float kf[U][8], vf[U][8];
-        bool valid[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const uint32_t pos = p0 + u * KPW + grp;
-            valid[u] = pos < pend;
-            if (valid[u] && dvalid) {
-                unpack8<T>(*reinterpret_cast<const Vec8*>(kbase + (uint64_t)pos * row_pitch), kf[u]);
-                unpack8<T>(*reinterpret_cast<const Vec8*>(vbase + (uint64_t)pos * row_pitch), vf[u]);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 8; ++e) kf[u][e] = vf[u][e] = 0.0f;
+
+    if (warp == NW) {
+        // Producer: one lane streams the K/V tiles of [pbeg, pend).
+        if (lane == 0 && ntiles > 0) {
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            const uint32_t bytes = tile_elems * 2 * sizeof(T);
+            uint32_t issued = 0;
+            for (uint32_t t = 0; t < ntiles; ++t) {
+                const uint32_t s = t % stages;
+                if (!mbar_wait(&empty[s], ((t / stages) & 1) ^ 1, s_abort, err, kTimeoutDecode)) break;
+                mbar_arrive_expect_tx(&full[s], bytes);
+                T* kt = reinterpret_cast<T*>(ring) + (size_t)s * 2 * tile_elems;
+                const int y = (int)((uint64_t)b * max_len + pbeg + t * ROWS);
+                tma_load_3d(kt, &tmK, &full[s], (int)(g * Dh), y, 0);
+                tma_load_3d(kt + tile_elems, &tmV, &full[s], (int)(g * Dh), y, 0);
+                issued = t + 1;
+            }
+            if (*s_abort) {
+                // Let the copies still in flight land before the CTA exits.
+                const uint32_t first = issued > stages ? issued - stages : 0;
+                for (uint32_t t = first; t < issued; ++t) mbar_drain(&full[t % stages], (t / stages) & 1);
             }
         }
+    } else {
+        float qf[G][8];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
+        for (int i = 0; i < G; ++i) {
+            if (i < (int)nh && dvalid) {
+                unpack8<T>(*reinterpret_cast<const Vec8*>(q + ((uint64_t)b * H + h0 + i) * Dh + d0), qf[i]);
 #pragma unroll
-            for (int i = 0; i < G; ++i) {
-                if (i >= (int)nh) break;
-                float sdot = 0.0f;
+                for (int e = 0; e < 8; ++e) qf[i][e] *= scale_log2;
+            } else {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) sdot = fmaf(qf[i][e], kf[u][e], sdot);
+                for (int e = 0; e < 8; ++e) qf[i][e] = 0.0f;
+            }
+        }
+        for (uint32_t t = 0; t < ntiles; ++t) {
+            const uint32_t s = t % stages;
+            // Every lane waits; the warp proceeds only if all of them saw the tile.
+            const bool ok = mbar_wait(&full[s], (t / stages) & 1, s_abort, err, kTimeoutDecode);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            const T* kt = reinterpret_cast<const T*>(ring) + (size_t)s * 2 * tile_elems;
+            const T* vt = kt + tile_elems;
+            const uint32_t r0 = warp * (KPW * STEPS) + grp;   // this lane group's first row
+            const uint32_t pos0 = pbeg + t * ROWS + r0;
+            // Rows are folded in blocks of SB steps, one rescale per block
+            // (SB < STEPS bounds the registers when many heads share the CTA).
+            constexpr int SB = (G >= 4 && STEPS > 2) ? 2 : STEPS;
 #pragma unroll
-                for (int off = LPK / 2; off > 0; off >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, off);
-                if (valid[u]) {
-                    const float mn = fmaxf(m[i], sdot);
-                    const float a = ex2f(m[i] - mn);
-                    const float p = ex2f(sdot - mn);
-                    l[i] = l[i] * a + p;
+            for (int jb = 0; jb < STEPS; jb += SB) {
+                float sd[SB][G];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) o[i][e] = fmaf(o[i][e], a, p * vf[u][e]);
-                    m[i] = mn;
+                for (int j = 0; j < SB; ++j) {
+                    float kf[8];
+                    if (dvalid) {
+                        unpack8<T>(*reinterpret_cast<const Vec8*>(kt + (r0 + (jb + j) * KPW) * Dh + d0), kf);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) kf[e] = 0.0f;
+                    }
+#pragma unroll
+                    for (int i = 0; i < G; ++i) {
+                        float d = 0.0f;
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) d = fmaf(qf[i][e], kf[e], d);
+                        sd[j][i] = d;
+                    }
                 }
+#pragma unroll
+                for (int off = LPK / 2; off > 0; off >>= 1)
+#pragma unroll
+                    for (int j = 0; j < SB; ++j)
+#pragma unroll
+                        for (int i = 0; i < G; ++i) sd[j][i] += __shfl_xor_sync(0xffffffffu, sd[j][i], off);
+#pragma unroll
+                for (int i = 0; i < G; ++i) {
+                    float mx = -INFINITY;
+#pragma unroll
+                    for (int j = 0; j < SB; ++j)
+                        if (pos0 + (jb + j) * KPW < pend) mx = fmaxf(mx, sd[j][i]);
+                    const float mn = fmaxf(m[i], mx);
+                    const float a = mn == -INFINITY ? 1.0f : ex2f(m[i] - mn);
+                    float ps = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < SB; ++j) {
+                        sd[j][i] = (pos0 + (jb + j) * KPW < pend) ? ex2f(sd[j][i] - mn) : 0.0f;
+                        ps += sd[j][i];
+                    }
+                    l[i] = l[i] * a + ps;
+                    m[i] = mn;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o[i][e] *= a;
+                }
+#pragma unroll
+                for (int j = 0; j < SB; ++j) {
+                    float vf[8];
+                    if (dvalid) {
+                        unpack8<T>(*reinterpret_cast<const Vec8*>(vt + (r0 + (jb + j) * KPW) * Dh + d0), vf);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) vf[e] = 0.0f;
+                    }
+#pragma unroll
+                    for (int i = 0; i < G; ++i)
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) o[i][e] = fmaf(sd[j][i], vf[e], o[i][e]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        // Merge the KPW row groups of the warp (lanes with equal `sub`).
+#pragma unroll
+        for (int i = 0; i < G; ++i) {
+            if (i >= (int)nh) break;
+#pragma unroll
+            for (int off = LPK; off < 32; off <<= 1) {
+                float m2 = __shfl_xor_sync(0xffffffffu, m[i], off);
+                float l2 = __shfl_xor_sync(0xffffffffu, l[i], off);
+                float mn = fmaxf(m[i], m2);
+                float a = mn == -INFINITY ? 0.0f : ex2f(m[i] - mn);
+                float a2 = mn == -INFINITY ? 0.0f : ex2f(m2 - mn);
+                l[i] = l[i] * a + l2 * a2;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    float o2 = __shfl_xor_sync(0xffffffffu, o[i][e], off);
+                    o[i][e] = o[i][e] * a + o2 * a2;
+                }
+                m[i] = mn;
             }
         }
     }
-    // Merge the KPW row groups of the warp (lanes with equal `sub`).
+    // All tiles are consumed (or the CTA gave up and the producer drained its
+    // copies): the ring now holds the warps' o partials.
+    __syncthreads();
+    if (warp < NW && grp == 0) {
 #pragma unroll
-    for (int i = 0; i < G; ++i) {
-        if (i >= (int)nh) break;
-#pragma unroll
-        for (int off = LPK; off < 32; off <<= 1) {
-            float m2 = __shfl_xor_sync(0xffffffffu, m[i], off);
-            float l2 = __shfl_xor_sync(0xffffffffu, l[i], off);
-            float mn = fmaxf(m[i], m2);
-            float a = mn == -INFINITY ? 0.0f : ex2f(m[i] - mn);
-            float a2 = mn == -INFINITY ? 0.0f : ex2f(m2 - mn);
-            l[i] = l[i] * a + l2 * a2;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                float o2 = __shfl_xor_sync(0xffffffffu, o[i][e], off);
-                o[i][e] = o[i][e] * a + o2 * a2;
-            }
-            m[i] = mn;
-        }
-        if (grp == 0) {
+        for (int i = 0; i < G; ++i) {
+            if (i >= (int)nh) break;
             if (sub == 0) {
                 sm_m[warp][i] = m[i];
                 sm_l[warp][i] = l[i];
             }
+            if (dvalid) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) sm_o[warp][i][d0 + e] = o[i][e];
+                for (int e = 0; e < 8; ++e) sm_o[warp][i][d0 + e] = o[i][e];
+            }
         }
     }
     __syncthreads();
@@ -193,15 +296,34 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     // Merge the splits and write o / l.
     for (uint32_t c = threadIdx.x; c < ncell; c += blockDim.x) {
         const uint32_t i = c / Dh, d = c % Dh;
-        const volatile float* pr = pbase + (uint64_t)i * nsplit * (Dh + 2);
+        // Partials come from other CTAs: read them from L2 (.cg), eight
+        // splits per batch so the loads overlap; merge in split order.
+        const float* pr = pbase + (uint64_t)i * nsplit * (Dh + 2);
         float mm = -INFINITY;
-        for (uint32_t s = 0; s < nsplit; ++s) mm = fmaxf(mm, pr[s * (Dh + 2)]);
+        for (uint32_t s0 = 0; s0 < nsplit; s0 += 8) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (s0 + j < nsplit) mm = fmaxf(mm, __ldcg(pr + (s0 + j) * (Dh + 2)));
+        }
         float ll = 0.0f, acc = 0.0f;
-        for (uint32_t s = 0; s < nsplit; ++s) {
-            float ms = pr[s * (Dh + 2)];
-            float a = mm == -INFINITY ? 0.0f : ex2f(ms - mm);
-            ll += pr[s * (Dh + 2) + 1] * a;
-            acc += pr[s * (Dh + 2) + 2 + d] * a;
+        for (uint32_t s0 = 0; s0 < nsplit; s0 += 8) {
+            float ms[8], ls[8], os[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const bool in = s0 + j < nsplit;
+                const float* p = pr + (s0 + j) * (Dh + 2);
+                ms[j] = in ? __ldcg(p) : -INFINITY;
+                ls[j] = in ? __ldcg(p + 1) : 0.0f;
+                os[j] = in ? __ldcg(p + 2 + d) : 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (s0 + j < nsplit) {
+                    const float a = mm == -INFINITY ? 0.0f : ex2f(ms[j] - mm);
+                    ll += ls[j] * a;
+                    acc += os[j] * a;
+                }
+            }
         }
         float v = ll > 0.0f ? acc / ll : 0.0f;
         out[((uint64_t)b * H + h0 + i) * Dh + d] = Elem<T>::from_f(v);
@@ -213,30 +335,62 @@ template <typename T, int LPK>
 int launch_decode(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t H, uint32_t Hkv,
                   uint32_t Dh, uint32_t max_len, uint32_t cur_len, const uint32_t* d_cur_len, float scale_log2,
                   cudaStream_t st) {
+    constexpr int ROWS = DecTile<LPK>::ROWS;
     DeviceState* ds = state();
     const uint32_t Gq = H / Hkv;
     const uint32_t hgroups = (Gq + kMaxGroup - 1) / kMaxGroup;  // same grouping for G = 1 (Gq = 1)
     const uint64_t ctas_wo_split = (uint64_t)B * Hkv * hgroups;
-    // Split positions so that the grid covers ~4 CTAs per SM, at least 64 rows each.
-    uint64_t want = std::max<uint64_t>(1, (4ull * ds->sm_count + ctas_wo_split - 1) / ctas_wo_split);
-    uint32_t chunk = (uint32_t)std::max<uint64_t>(64, (cur_len + want - 1) / want);
-    chunk = (chunk + 31) / 32 * 32;
+    if (ctas_wo_split > kMaxTickets) return fail(EVKCU_BAD_SHAPE, "evkcu_single_query_attention: B*Hkv too large");
+    auto kern = Gq == 1 ? decode_attn_kernel<T, LPK, 1> : decode_attn_kernel<T, LPK, kMaxGroup>;
+    // Ring: as many K/V tile pairs as fit the per-CTA target (at least 2);
+    // where registers allow only one CTA per SM, a deeper ring instead.
+    const uint32_t stage_bytes = 2u * ROWS * Dh * 2;
+    const uint32_t obytes = (uint32_t)(kDecCompute * (Gq == 1 ? 1 : kMaxGroup) * LPK * 8 * sizeof(float));
+    auto ring_bytes = [&](uint32_t target, uint32_t* stages) {
+        *stages = std::max<uint32_t>(2, std::min<uint32_t>(kMaxStages, target / stage_bytes));
+        return std::max(*stages * stage_bytes, obytes);
+    };
+    uint32_t stages = 0;
+    uint32_t smem = ring_bytes(kDecSmemTarget, &stages);
+    // Per kernel variant: the attribute once, the occupancy per ring size.
+    static bool attr_set[2] = {false, false};
+    static uint32_t occ_smem[2] = {0, 0};
+    static int occ_blocks[2] = {0, 0};
+    const int vi = Gq == 1 ? 0 : 1;
+    if (!attr_set[vi]) {
+        EVKCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        attr_set[vi] = true;
+    }
+    if (occ_smem[vi] != smem) {
+        EVKCU_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_blocks[vi], kern, kDecThreads, smem));
+        occ_smem[vi] = smem;
+    }
+    int per_sm = occ_blocks[vi];
+    if (per_sm <= 1) {
+        smem = ring_bytes(192 * 1024, &stages);
+        per_sm = 1;
+    }
+    // One resident wave: split positions over the CTA slots left per (b, g, head group).
+    const uint64_t slots = (uint64_t)per_sm * ds->sm_count;
+    const uint64_t want = std::max<uint64_t>(1, slots / ctas_wo_split);
+    uint32_t chunk = (uint32_t)std::max<uint64_t>(ROWS, (cur_len + want - 1) / want);
+    chunk = (chunk + ROWS - 1) / ROWS * ROWS;
     const uint32_t nsplit = (cur_len + chunk - 1) / chunk;
     const size_t pbytes = (size_t)B * H * nsplit * (Dh + 2) * sizeof(float);
-    if (ctas_wo_split > kMaxTickets) return fail(EVKCU_BAD_SHAPE, "evkcu_single_query_attention: B*Hkv too large");
-    const size_t toff = kTicketBytes;
-    char* ws = (char*)workspace(WS_DECODE, toff + pbytes);
+    char* ws = (char*)workspace(WS_DECODE, kTicketBytes + pbytes);
     if (!ws) return fail(EVKCU_CUDA_ERROR, "evkcu_single_query_attention: scratch allocation failed");
+    // The caches as [B * max_len rows, Hkv * Dh] matrices; a box is Dh x ROWS.
+    CUtensorMap mK, mV;
+    const uint64_t pitch = (uint64_t)Hkv * Dh, rows = (uint64_t)B * max_len;
+    const int dt = std::is_same<T, __nv_bfloat16>::value ? EVKCU_BF16 : EVKCU_F16;
+    int r = make_tmap_3d(&mK, k, pitch, rows, 1, pitch, pitch * rows, Dh, ROWS, dt, false);
+    if (r) return r;
+    r = make_tmap_3d(&mV, v, pitch, rows, 1, pitch, pitch * rows, Dh, ROWS, dt, false);
+    if (r) return r;
     dim3 grid(nsplit, Hkv * hgroups, B);
-    // MHA (one query head per cached head) needs no head group registers.
-    if (Gq == 1)
-        decode_attn_kernel<T, LPK, 1><<<grid, kDecThreads, 0, st>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, H,
-                                                                   Hkv, Dh, max_len, cur_len, d_cur_len, chunk,
-                                                                   scale_log2, (float*)(ws + toff), (unsigned int*)ws);
-    else
-        decode_attn_kernel<T, LPK, kMaxGroup><<<grid, kDecThreads, 0, st>>>(
-            (const T*)q, (const T*)k, (const T*)v, (T*)o, H, Hkv, Dh, max_len, cur_len, d_cur_len, chunk, scale_log2,
-            (float*)(ws + toff), (unsigned int*)ws);
+    kern<<<grid, kDecThreads, smem, st>>>(mK, mV, (const T*)q, (T*)o, H, Hkv, Dh, max_len, cur_len, d_cur_len, chunk,
+                                          scale_log2, stages, (float*)(ws + kTicketBytes), (unsigned int*)ws,
+                                          ds->d_error);
     return after_launch("evkcu_single_query_attention");
 }
 

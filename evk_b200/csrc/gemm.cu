@@ -348,9 +348,18 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
     const float* base = partial + (uint64_t)blockIdx.x * gridDim.y * (GV_MMA_N * GV_COLS);
     for (uint32_t i = threadIdx.x; i < Mt * GV_COLS; i += blockDim.x) {
         const uint32_t m = i / GV_COLS, c = i % GV_COLS, n = n0 + c;
+        // Partials are read from L2 (.cg: written by other CTAs) eight at a
+        // time, then added in split order.
         float sum = 0.0f;
-        for (uint32_t y = 0; y < gridDim.y; ++y)
-            sum += ((volatile const float*)base)[(uint64_t)y * (GV_MMA_N * GV_COLS) + i];
+        for (uint32_t y0 = 0; y0 < gridDim.y; y0 += 8) {
+            float t[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                t[j] = y0 + j < gridDim.y ? __ldcg(base + (uint64_t)(y0 + j) * (GV_MMA_N * GV_COLS) + i) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (y0 + j < gridDim.y) sum += t[j];
+        }
         if (n < N) {
             if (acc_c) sum += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
             Y[(uint64_t)m * N + n] = Elem<T>::from_f(sum);

@@ -73,6 +73,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// Bounded wait that ignores the abort flags: used on the way out of a kernel
+// that gave up, to let its own TMA copies land before the CTA exits.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    const long long t0 = clock64();
+    while (!mbar_try_wait(a, parity) && clock64() - t0 < kSpinLimitCycles / 4) {
+    }
+}
+
 // ------------------------------------------------------------------ TMA ----
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
@@ -194,10 +203,11 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t M, uint32_t N, ui
 
 }  // namespace sm100
 
-// Host: encodes a 3-D tiled tensor map with 128-byte swizzle through the driver
-// entry point (no link-time dependency on libcuda).  dims/strides in elements
-// of 2 bytes; box in elements.  Returns EVKCU_OK or an error status.
+// Host: encodes a 3-D tiled tensor map through the driver entry point (no
+// link-time dependency on libcuda), 128-byte swizzled by default, else a
+// dense row-major box.  dims/strides in elements of 2 bytes; box in elements.
+// Returns EVKCU_OK or an error status.
 int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_elems,
-                 uint64_t stride2_elems, uint32_t box0, uint32_t box1, int dtype);
+                 uint64_t stride2_elems, uint32_t box0, uint32_t box1, int dtype, bool swizzle128 = true);
 
 }  // namespace evkcu

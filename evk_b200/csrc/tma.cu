@@ -23,7 +23,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t stride1_elems,
-                 uint64_t stride2_elems, uint32_t box0, uint32_t box1, int dtype) {
+                 uint64_t stride2_elems, uint32_t box0, uint32_t box1, int dtype, bool swizzle128) {
     auto fn = encode_fn();
     if (!fn) return fail(EVKCU_CUDA_ERROR, "cuTensorMapEncodeTiled entry point unavailable");
     if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return fail(EVKCU_BAD_ALIGN, "TMA base not 16-byte aligned");
@@ -35,7 +35,7 @@ int make_tmap_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, u
     cuuint32_t estride[3] = {1, 1, 1};
     CUtensorMapDataType dt = dtype == EVKCU_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS)
         return fail(EVKCU_BAD_SHAPE, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string((int)r));
