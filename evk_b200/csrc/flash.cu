@@ -9,9 +9,9 @@
 // [B, N, Hkv*Dh] (the reference call is Hkv = 1, non-causal).
 //
 // tcgen05 kernel (Dh = 64 or 128): one CTA per NT consecutive 128-query
-// tiles of one (batch, head); see flash_tc_kernel for the warp roles.  S and
-// O live in TMEM; P goes through shared memory as the A operand of the PV
-// MMA; O is rescaled lazily (FlashAttention-4 style) only when a row's
+// tiles of one (batch, head); see flash_tc_kernel for the warp roles.  S, O
+// and P live in TMEM (P is the TMEM-resident A operand of the PV MMA, so
+// shared-memory bandwidth is left to the Q/K/V operands); O is rescaled lazily (FlashAttention-4 style) only when a row's
 // running max grows by more than 2^8.  Causal tiles stop at the diagonal
 // block; only diagonal / ragged blocks evaluate the mask.
 //
@@ -40,20 +40,28 @@ template <int DH, int NT>
 struct FlashCfg {
     static constexpr int Q_BYTES = FM * DH * 2;  // per tile
     static constexpr int KV_BYTES = FN * DH * 2;  // one K or V block
-    static constexpr int P_BYTES = FM * FN * 2;  // per tile
-    static constexpr int STAGES = NT == 2 ? 3 : (DH == 64 ? 4 : 2);
+    static constexpr int STAGES = NT == 2 ? 5 : (DH == 64 ? 6 : 3);
     static constexpr int OFF_Q = 0;
-    static constexpr int OFF_P = OFF_Q + NT * Q_BYTES;
-    static constexpr int OFF_K = OFF_P + NT * P_BYTES;
+    static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
     static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
     static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;
     static constexpr int THREADS = 128 + NT * 128;
-    static constexpr uint32_t TMEM_COLS = NT == 2 ? 512 : 256;
-    // tile t: S (fp32, 128 cols) at t*256, O (fp32, DH cols) at t*256 + 128
+    static constexpr uint32_t TMEM_COLS = 512;
+    // Per tile t: S (fp32, FN columns), O (fp32, DH columns) and P (FN 16-bit
+    // values packed two per column, FN/2 columns).
     static __device__ __forceinline__ uint32_t col_s(int t) { return t * 256; }
-    static __device__ __forceinline__ uint32_t col_o(int t) { return t * 256 + 128; }
+    static __device__ __forceinline__ uint32_t col_o(int t) { return t * 256 + FN; }
+    static __device__ __forceinline__ uint32_t col_p(int t) { return NT == 2 ? t * 256 + FN + DH : FN + DH; }
 };
+static_assert(FlashCfg<64, 2>::SMEM <= 227 * 1024 && FlashCfg<128, 1>::SMEM <= 227 * 1024, "flash smem");
+
+// max(a, b, c) in one instruction (sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
 
 __device__ __forceinline__ float ex2(float x) {
     float y;
@@ -78,14 +86,6 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     return *reinterpret_cast<float2*>(&d);
 }
 
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, const Vec8& v) {
-    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.w[0]), "r"(v.w[1]), "r"(v.w[2]),
-                 "r"(v.w[3])
-                 : "memory");
-}
-
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
 // Persistent kernel: one CTA per SM walks work items in zig-zag rounds
 // (see item_of); an item is NT consecutive 128-query tiles of
 // one (batch, head), heaviest causal items first.  Barriers, TMEM and the
@@ -94,14 +94,17 @@ __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.a
 //   warp 0       TMA producer: per item, Q tiles (once the previous item's S
 //                MMAs are done: q_empty), then K_j / V_j into a STAGES ring
 //                whose index runs across items.
-//   warp 1       TMEM owner + MMA issuer, event-driven per tile: S_t(j) =
-//                Q_t K_j^T once K_j is loaded and softmax t has read S_t(j-1);
-//                O_t += P_t(j) V_j once P_t(j) is written (the first PV of an
-//                item also waits until the previous item's O_t was read out).
-//   warps 2-3    idle.
+//   warp 1       TMEM owner + S issuer: S_t(j) = Q_t K_j^T once K_j is
+//                loaded and softmax t has read S_t(j-1).
+//   warp 2       PV issuer: O_t += P_t(j) V_j once P_t(j) is in TMEM (the
+//                first PV of an item also waits until the previous item's O_t
+//                was read out).  tcgen05.mma issue holds the issuing thread
+//                for about the MMAs' execution time, so the two streams get
+//                their own warps and neither waits behind the other.
+//   warp 3       idle.
 //   warpgroup 1+t  softmax of tile t, one thread per query row (= TMEM lane):
-//                one TMEM load of the S row, row max, P = exp2 into shared
-//                memory (128-byte-swizzled K-major, the A operand of the PV
+//                one TMEM load of the S row, row max, P = exp2 packed to
+//                16-bit pairs and stored to TMEM (the A operand of the PV
 //                MMA), lazy rescale of the O row in TMEM only when the running
 //                max grows by > 2^8, finally O / l from TMEM to global memory.
 // Every barrier is waited on (or probed) for exactly one completion at a time,
@@ -118,7 +121,6 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem + Cfg::OFF_Q;
-    uint8_t* sP = smem + Cfg::OFF_P;
     uint8_t* sK = smem + Cfg::OFF_K;
     uint8_t* sV = smem + Cfg::OFF_V;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
@@ -167,7 +169,7 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
         for (int s = 0; s < ST; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&v_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&kv_empty[s], 2);
         }
         for (int t = 0; t < NT; ++t) {
             mbar_init(&s_full[t], 1);
@@ -237,43 +239,50 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
                 }
             }
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------- MMA issuer ----
-        if (lane == 0) {
-            const uint32_t qaddr = smem_u32(sQ);
-            const uint32_t paddr = smem_u32(sP);
-            uint32_t rbase = 0, it = 0;
-            uint32_t gs[NT], ep[NT];  // per tile: blocks processed before this item, epilogues finished
+    } else if (warp == 1 || warp == 2) {
+        // ------------------------------------------------ MMA issuers ----
+        // Warp 1 issues every S MMA, warp 2 every PV MMA, each in a static
+        // order over the item's blocks.  S_t(j) waits for K_j and for softmax
+        // t to have read S_t(j-1); PV_t(j) waits for P_t(j), V_j and (first
+        // block of an item) for O_t to have been read out.  The two streams
+        // write disjoint TMEM (S vs O) and meet only through the softmax
+        // barriers, so neither waits behind the other's events.  Waits block
+        // (lane 0 sleeps in try_wait, the other lanes at the broadcast), one
+        // elected lane issues.  A ring slot is released by one commit from
+        // each issuer (kv_empty counts 2).
+        const bool is_s = warp == 1;
+        const bool leader = elect_one();
+        const uint32_t qaddr = smem_u32(sQ);
+        uint32_t rbase = 0, it = 0;
+        uint32_t gs[NT], ep[NT];  // per tile: blocks processed before this item, epilogues finished
 #pragma unroll
-            for (int t = 0; t < NT; ++t) gs[t] = ep[t] = 0;
-            bool ok = true;
-            long long idle_since = clock64();
-            for (uint32_t rd = 0; ok && rd * gridDim.x < items; ++rd) {
-                const uint32_t w = item_of(rd);
-                if (w >= items) continue;
-                uint32_t b, h, q0[NT], nblk[NT];
-                item_geom(w, b, h, q0, nblk);
-                uint32_t nmax = 0;
+        for (int t = 0; t < NT; ++t) gs[t] = ep[t] = 0;
+        bool ok = true;
+        auto probe = [&](bool c) { return __shfl_sync(0xffffffffu, (int)c, 0) != 0; };
+        for (uint32_t rd = 0; ok && rd * gridDim.x < items; ++rd) {
+            const uint32_t w = item_of(rd);
+            if (w >= items) continue;
+            uint32_t b, h, q0[NT], nblk[NT];
+            item_geom(w, b, h, q0, nblk);
+            uint32_t nmax = 0;
 #pragma unroll
-                for (int t = 0; t < NT; ++t) nmax = max(nmax, nblk[t]);
-                if (!mbar_wait(q_full, it & 1, s_abort, err, kTimeoutFlash)) break;
-                tc_fence_after();
-                uint32_t ns[NT], np[NT];
-#pragma unroll
-                for (int t = 0; t < NT; ++t) ns[t] = np[t] = 0;
-                uint32_t released = 0;
-                bool q_released = false;
-                while (true) {
-                    bool done = true, progress = false;
+            for (int t = 0; t < NT; ++t) nmax = max(nmax, nblk[t]);
+            if (is_s && !probe(lane == 0 && mbar_wait(q_full, it & 1, s_abort, err, kTimeoutFlash))) break;
+            tc_fence_after();
+            for (uint32_t j = 0; ok && j < nmax; ++j) {
+                const uint32_t r = rbase + j;
+                if (is_s) {
+                    ok = probe(lane == 0 && mbar_wait(&k_full[r % ST], (r / ST) & 1, s_abort, err, kTimeoutFlash));
+                    const uint32_t kaddr = smem_u32(sK + (r % ST) * Cfg::KV_BYTES);
 #pragma unroll
                     for (int t = 0; t < NT; ++t) {
-                        if (np[t] < nblk[t]) done = false;
-                        const uint32_t j = ns[t];
                         const uint32_t gj = gs[t] + j;  // tile-global block index
-                        if (j < nblk[t] && mbar_try_wait(smem_u32(&k_full[(rbase + j) % ST]), ((rbase + j) / ST) & 1) &&
-                            (gj == 0 || mbar_try_wait(smem_u32(&s_free[t]), (gj - 1) & 1))) {
-                            tc_fence_after();
-                            const uint32_t kaddr = smem_u32(sK + ((rbase + j) % ST) * Cfg::KV_BYTES);
+                        if (!ok || j >= nblk[t]) continue;
+                        ok = gj == 0 || probe(lane == 0 && mbar_wait(&s_free[t], (gj - 1) & 1, s_abort, err,
+                                                                     kTimeoutFlash));
+                        if (!ok) break;
+                        tc_fence_after();
+                        if (leader) {
 #pragma unroll
                             for (int kk = 0; kk < DH / 16; ++kk) {
                                 uint64_t ad = make_sw128_desc(
@@ -282,72 +291,48 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
                                 mma_f16_ss(tmem + Cfg::col_s(t), ad, bd, idesc_s, kk != 0);
                             }
                             mma_commit(&s_full[t]);
-                            ns[t] = j + 1;
-                            progress = true;
                         }
-                        const uint32_t jj = np[t];
-                        const uint32_t gjj = gs[t] + jj;
-                        if (jj < ns[t] && mbar_try_wait(smem_u32(&p_full[t]), gjj & 1) &&
-                            mbar_try_wait(smem_u32(&v_full[(rbase + jj) % ST]), ((rbase + jj) / ST) & 1) &&
-                            (jj != 0 || ep[t] == 0 || mbar_try_wait(smem_u32(&o_free[t]), (ep[t] - 1) & 1))) {
-                            tc_fence_after();
-                            const uint32_t vaddr = smem_u32(sV + ((rbase + jj) % ST) * Cfg::KV_BYTES);
+                        __syncwarp();
+                    }
+                    if (!ok) break;
+                    // Q is free once every S of this item has completed.
+                    if (j + 1 == nmax && leader) mma_commit(q_empty);
+                } else {
+                    ok = probe(lane == 0 && mbar_wait(&v_full[r % ST], (r / ST) & 1, s_abort, err, kTimeoutFlash));
+                    const uint32_t vaddr = smem_u32(sV + (r % ST) * Cfg::KV_BYTES);
+#pragma unroll
+                    for (int t = 0; t < NT; ++t) {
+                        const uint32_t gj = gs[t] + j;
+                        if (!ok || j >= nblk[t]) continue;
+                        ok = probe(lane == 0 && mbar_wait(&p_full[t], gj & 1, s_abort, err, kTimeoutFlash) &&
+                                   (j != 0 || ep[t] == 0 ||
+                                    mbar_wait(&o_free[t], (ep[t] - 1) & 1, s_abort, err, kTimeoutFlash)));
+                        if (!ok) break;
+                        tc_fence_after();
+                        if (leader) {
 #pragma unroll
                             for (int kk = 0; kk < FN / 16; ++kk) {
-                                uint64_t ad = make_sw128_desc(
-                                    paddr + t * Cfg::P_BYTES + (kk >> 2) * (FM * 128) + (kk & 3) * 32, 16, 1024);
+                                // A = P_t from TMEM: 16 keys = 8 packed columns per MMA.
                                 uint64_t bd = make_sw128_desc(vaddr + kk * 2048, FN * 128, 1024);
-                                mma_f16_ss(tmem + Cfg::col_o(t), ad, bd, idesc_pv, (jj | kk) != 0);
+                                mma_f16_ts(tmem + Cfg::col_o(t), tmem + Cfg::col_p(t) + kk * 8, bd, idesc_pv,
+                                           (j | kk) != 0);
                             }
                             mma_commit(&pv_done[t]);
-                            np[t] = jj + 1;
-                            progress = true;
                         }
+                        __syncwarp();
                     }
-                    // Q is free once every S of this item has been issued (the
-                    // commit fires when those MMAs have completed).
-                    if (!q_released) {
-                        bool all_s = true;
-#pragma unroll
-                        for (int t = 0; t < NT; ++t) all_s = all_s && ns[t] == nblk[t];
-                        if (all_s) {
-                            mma_commit(q_empty);
-                            q_released = true;
-                        }
-                    }
-                    // Hand back ring slots whose block every tile has consumed.
-                    while (released < nmax) {
-                        bool all = true;
-#pragma unroll
-                        for (int t = 0; t < NT; ++t)
-                            if (released < nblk[t] && np[t] <= released) all = false;
-                        if (!all) break;
-                        mma_commit(&kv_empty[(rbase + released) % ST]);
-                        ++released;
-                    }
-                    if (done) break;
-                    if (progress) {
-                        idle_since = clock64();
-                    } else if (*s_abort || *reinterpret_cast<volatile unsigned int*>(err)) {
-                        *s_abort = 1;
-                        ok = false;
-                        break;
-                    } else if (clock64() - idle_since > kSpinLimitCycles) {
-                        *s_abort = 1;
-                        atomicCAS(err, 0u, kTimeoutFlash);
-                        ok = false;
-                        break;
-                    } else {
-                        __nanosleep(32);  // leave issue slots to the softmax warps on this scheduler
-                    }
+                    if (!ok) break;
                 }
-                ++it;
-                rbase += nmax;
+                // This issuer is done with ring slot j once its MMAs complete.
+                if (leader) mma_commit(&kv_empty[r % ST]);
+                __syncwarp();
+            }
+            ++it;
+            rbase += nmax;
 #pragma unroll
-                for (int t = 0; t < NT; ++t) {
-                    gs[t] += nblk[t];
-                    if (nblk[t] > 0) ++ep[t];
-                }
+            for (int t = 0; t < NT; ++t) {
+                gs[t] += nblk[t];
+                if (nblk[t] > 0) ++ep[t];
             }
         }
     } else if (warp >= 4) {
@@ -358,7 +343,7 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
         const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
         const uint32_t s_addr = lane_addr + Cfg::col_s(t);
         const uint32_t o_addr = lane_addr + Cfg::col_o(t);
-        const uint32_t prow = smem_u32(sP + t * Cfg::P_BYTES + row * 128);
+        const uint32_t p_addr = lane_addr + Cfg::col_p(t);
         uint32_t gbase = 0;  // blocks this tile processed in earlier items
         bool ok = true;
         for (uint32_t rd = 0; ok && rd * gridDim.x < items; ++rd) {
@@ -389,42 +374,33 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
 
                 const uint32_t k0 = j * FN;
                 const bool need_mask = (k0 + FN > N) || (causal && j + 1 == nb);
-                // Row max with 8 independent accumulators.
-                float mxa[8];
+                // Row max: three-input max, four independent accumulators.
+                float mxa[4];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) mxa[i] = -INFINITY;
+                for (int i = 0; i < 4; ++i) mxa[i] = -INFINITY;
                 if (need_mask) {
 #pragma unroll
                     for (int c = 0; c < FN / 32; ++c)
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) {
+                        for (int e = 0; e < 32; ++e)
                             if (k0 + c * 32 + e >= kmax) sr[c][e] = __float_as_uint(-INFINITY);
-                            mxa[e & 7] = fmaxf(mxa[e & 7], __uint_as_float(sr[c][e]));
-                        }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < FN / 32; ++c)
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) mxa[e & 7] = fmaxf(mxa[e & 7], __uint_as_float(sr[c][e]));
                 }
-                const float mx = fmaxf(fmaxf(fmaxf(mxa[0], mxa[1]), fmaxf(mxa[2], mxa[3])),
-                                       fmaxf(fmaxf(mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7])));
+#pragma unroll
+                for (int c = 0; c < FN / 32; ++c)
+#pragma unroll
+                    for (int e = 0; e < 32; e += 2)
+                        mxa[(e >> 1) & 3] = fmax3(mxa[(e >> 1) & 3], __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+                const float mx = fmax3(fmaxf(mxa[0], mxa[1]), mxa[2], mxa[3]);
                 const float m_cand = fmaxf(m_ref, mx * scale_log2);
                 // Lazy rescale: keep the reference max unless it grew by > 2^8.
                 const bool need = j > 0 && m_cand > m_ref + kRescaleThreshold;
                 const float alpha = need ? ex2(m_ref - m_cand) : 1.0f;  // m_ref = -inf -> 0
                 if (j == 0 || need) m_ref = m_cand;
-                if (j > 0) {
-                    // PV_t(j-1) must be complete before the P buffer is reused
-                    // and before O is rescaled.
-                    if (!mbar_wait(&pv_done[t], (gj - 1) & 1, s_abort, err, kTimeoutFlash)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                }
                 const float m_use = (m_ref == -INFINITY) ? 0.0f : m_ref;
-                // p = exp2(s * scale_log2 - m) with packed fp32x2 scale-subtract and sums.
+                // p = exp2(s * scale_log2 - m) with packed fp32x2 scale-subtract
+                // and sums, packed to 16-bit pairs in place (sr[c][0..15]).
+                // This runs before waiting for PV_t(j-1), so the exponentials
+                // overlap that MMA.
                 const float2 sc2 = make_float2(scale_log2, scale_log2);
                 const float2 nm2 = make_float2(-m_use, -m_use);
                 float2 rs2[4];
@@ -444,10 +420,19 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
                             f[e + 1] = ex2(x.y);
                             rs2[e >> 1] = fadd2(rs2[e >> 1], make_float2(f[e], f[e + 1]));
                         }
-                        const int key = c * 32 + q * 8;
-                        const int chunk = (key & 63) >> 3;
-                        st_shared_v4(prow + (key >> 6) * (FM * 128) + ((chunk ^ (row & 7)) << 4), pack8<T>(f));
+                        const Vec8 pk = pack8<T>(f);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) sr[c][q * 4 + i] = pk.w[i];
                     }
+                }
+                if (j > 0) {
+                    // PV_t(j-1) must be complete before the P columns are
+                    // overwritten and before O is rescaled.
+                    if (!mbar_wait(&pv_done[t], (gj - 1) & 1, s_abort, err, kTimeoutFlash)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
                 }
                 const float rs = ((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y)) +
                                  ((rs2[2].x + rs2[2].y) + (rs2[3].x + rs2[3].y));
@@ -462,11 +447,17 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
                         for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
                         tmem_st32(o_addr + c * 32, rr);
                     }
-                    tmem_wait_st();
                 }
-                // P (shared-memory stores) and any O rescale must be visible to
-                // the tensor core before the PV MMA is issued.
-                fence_async_smem();
+#pragma unroll
+                for (int c = 0; c < FN / 32; ++c) {
+                    uint32_t pw[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) pw[i] = sr[c][i];
+                    tmem_st16(p_addr + c * 16, pw);
+                }
+                // P and any O rescale (TMEM stores) must be complete before
+                // the PV MMA is issued.
+                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[t]);
