@@ -9,6 +9,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/evkcu.h"
 
@@ -39,6 +40,17 @@ inline int after_launch(const char* what) {
     return EVKCU_OK;
 }
 
+// ------------------------------------------ programmatic dependent launch ----
+// Kernels on the decode path are launched with programmatic stream
+// serialization: the next kernel may start while this one drains, runs its
+// prologue (barrier setup, TMEM allocation, loads of constant weights) and
+// then waits in pdl_wait() until every earlier kernel has completed and its
+// writes are visible.  A kernel launched this way must not read data written
+// by an earlier kernel, nor write data an earlier kernel reads, before
+// pdl_wait().  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------ per-device state ----
 // Scratch slots: each op family that needs global scratch owns one, so ops on
 // different streams never share scratch.  Scratch is zero-filled when it is
@@ -51,6 +63,7 @@ struct DeviceState {
     unsigned int* d_error = nullptr;  // device error word for bounded waits
     void* ws[WS_COUNT] = {};
     size_t ws_bytes[WS_COUNT] = {};
+    bool pdl = true;  // programmatic dependent launch for the decode-path kernels
 };
 // Returns the state of the current device, creating it on first use.
 DeviceState* state();
@@ -67,6 +80,27 @@ constexpr size_t kTicketBytes = 256 * 1024;
 constexpr uint32_t kMaxTickets = kTicketBytes / sizeof(unsigned int);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Launches a kernel that calls pdl_wait() before its first dependent access,
+// with programmatic stream serialization unless disabled for the device.
+template <typename... KArgs, typename... Args>
+int launch_pdl(const char* what, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    DeviceState* s = state();
+    cfg.attrs = attr;
+    cfg.numAttrs = (s && s->pdl) ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return after_launch(what);
+}
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -1,6 +1,7 @@
 // context.cu — per-device state, error reporting and launch accounting.
 // Replaces evk::ai::initialize/shutdown (evk_ai.cpp:211-252): there are no
 // pipelines to create, only a device error word and a reusable workspace.
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -46,6 +47,7 @@ DeviceState* state() {
         return nullptr;
     }
     cudaMemset(s->d_error, 0, sizeof(unsigned int));
+    if (const char* v = getenv("EVKCU_DISABLE_PDL")) s->pdl = v[0] == '\0' || v[0] == '0';
     g_states[dev] = s;
     return s;
 }

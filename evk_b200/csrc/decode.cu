@@ -59,6 +59,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     T* __restrict__ out, uint32_t H, uint32_t Hkv, uint32_t Dh, uint32_t max_len, uint32_t cur_len,
     const uint32_t* __restrict__ d_cur_len, uint32_t chunk, float scale_log2, uint32_t stages,
     float* __restrict__ partial, unsigned int* __restrict__ tickets, unsigned int* err) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     constexpr int KPW = DecTile<LPK>::KPW, ROWS = DecTile<LPK>::ROWS, STEPS = DecTile<LPK>::STEPS;
     constexpr int NW = kDecCompute;
     __shared__ float sm_m[NW][G], sm_l[NW][G];
@@ -388,10 +390,9 @@ int launch_decode(const void* q, const void* k, const void* v, void* o, uint32_t
     r = make_tmap_3d(&mV, v, pitch, rows, 1, pitch, pitch * rows, Dh, ROWS, dt, false);
     if (r) return r;
     dim3 grid(nsplit, Hkv * hgroups, B);
-    kern<<<grid, kDecThreads, smem, st>>>(mK, mV, (const T*)q, (T*)o, H, Hkv, Dh, max_len, cur_len, d_cur_len, chunk,
-                                          scale_log2, stages, (float*)(ws + kTicketBytes), (unsigned int*)ws,
-                                          ds->d_error);
-    return after_launch("evkcu_single_query_attention");
+    return launch_pdl("evkcu_single_query_attention", kern, grid, kDecThreads, smem, st, mK, mV, (const T*)q, (T*)o, H,
+                      Hkv, Dh, max_len, cur_len, d_cur_len, chunk, scale_log2, stages, (float*)(ws + kTicketBytes),
+                      (unsigned int*)ws, ds->d_error);
 }
 
 }  // namespace

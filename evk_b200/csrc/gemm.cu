@@ -253,13 +253,15 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
+    pdl_trigger();
+    // Every thread but the producer lane (which waits after requesting the
+    // first weight tiles) may read or write data of earlier kernels: x through
+    // the MMAs, y and the split scratch in the epilogue and final reduction.
+    if (warp != 0 || lane != 0) pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {
-            for (uint32_t i = 0; i < nkt; ++i) {
-                const int s = i % GV_STAGES;
-                if (!mbar_wait(&empty[s], ((i / GV_STAGES) & 1) ^ 1, s_abort, err, kTimeoutGemv)) break;
-                mbar_arrive_expect_tx(&full[s], GV_STAGE_BYTES);
+            auto load_w = [&](uint32_t i, int s) {
                 const int k0 = (int)((kt0 + i) * GV_BK);
                 uint8_t* w = sW + s * GV_W_BYTES;
                 if (W_KMAJOR) {
@@ -268,7 +270,23 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
                     tma_load_3d(w, &tmW, &full[s], (int)n0, k0, 0);
                     tma_load_3d(w + GV_W_BYTES / 2, &tmW, &full[s], (int)n0 + 64, k0, 0);
                 }
-                tma_load_3d(sX + s * GV_X_BYTES, &tmX, &full[s], k0, 0, 0);
+            };
+            // The weights are constant: the first ring of W tiles is requested
+            // before waiting for the kernels that produce x.
+            const uint32_t pre = min(nkt, (uint32_t)GV_STAGES);
+            for (uint32_t i = 0; i < pre; ++i) {
+                mbar_arrive_expect_tx(&full[i], GV_STAGE_BYTES);
+                load_w(i, (int)i);
+            }
+            pdl_wait();
+            for (uint32_t i = 0; i < pre; ++i)
+                tma_load_3d(sX + i * GV_X_BYTES, &tmX, &full[i], (int)((kt0 + i) * GV_BK), 0, 0);
+            for (uint32_t i = pre; i < nkt; ++i) {
+                const int s = i % GV_STAGES;
+                if (!mbar_wait(&empty[s], ((i / GV_STAGES) & 1) ^ 1, s_abort, err, kTimeoutGemv)) break;
+                mbar_arrive_expect_tx(&full[s], GV_STAGE_BYTES);
+                load_w(i, s);
+                tma_load_3d(sX + s * GV_X_BYTES, &tmX, &full[s], (int)((kt0 + i) * GV_BK), 0, 0);
             }
         }
     } else if (warp == 1) {
@@ -403,8 +421,8 @@ int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32
     }
     const uint32_t idesc = make_idesc_f16(GV_COLS, GV_MMA_N, dtype == EVKCU_BF16 ? 1 : 0, W_KMAJOR ? 0 : 1, 0);
     dim3 grid(slabs, splits);
-    kern<<<grid, GV_THREADS, GV_SMEM, st>>>(mW, mX, Y, Mt, K, N, per, acc, idesc, partial, tickets, s->d_error);
-    return after_launch("evkcu_matmul(gemv_tc)");
+    return launch_pdl("evkcu_matmul(gemv_tc)", kern, grid, GV_THREADS, GV_SMEM, st, mW, mX, Y, Mt, K, N, per, acc, idesc,
+                      partial, tickets, s->d_error);
 }
 
 template <typename T, int BN, bool A_MN, bool B_MN>

@@ -77,6 +77,8 @@ __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, uint32_t R, ui
                                        float base, T* __restrict__ q_out, T* __restrict__ k_out,
                                        T* __restrict__ v_out, T* __restrict__ kcache, T* __restrict__ vcache,
                                        uint32_t max_len) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     const uint32_t C = (Hq + 2 * Hk) * Dh;
     const uint32_t per_row = C / 8;
     const uint32_t p0 = d_pos ? *d_pos : pos0;
@@ -117,6 +119,8 @@ __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, uint32_t R, ui
 
 // After a decode step: one more cached position.
 __global__ void advance_kernel(uint32_t* d_pos, uint32_t* d_len) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     const uint32_t p = *d_pos + 1;
     *d_pos = p;
     *d_len = p + 1;
@@ -131,6 +135,8 @@ __global__ void set_pos_kernel(uint32_t* d_pos, uint32_t* d_len, uint32_t pos) {
 template <typename T>
 __global__ void argmax_key_kernel(const T* __restrict__ logits, uint32_t Vl, uint32_t voff,
                                   unsigned long long* __restrict__ keys) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     __shared__ unsigned long long sh[32];
     const T* row = logits + (uint64_t)blockIdx.x * Vl;
     unsigned long long best = 0;
@@ -159,6 +165,8 @@ __global__ void argmax_key_kernel(const T* __restrict__ logits, uint32_t Vl, uin
 // ids[b] = token of max_r keys[r * B + b] (token 0 when nothing is selectable).
 __global__ void keys_to_ids_kernel(const unsigned long long* __restrict__ keys, uint32_t ranks, uint32_t B,
                                    uint32_t* __restrict__ ids) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     unsigned long long best = 0;
@@ -243,11 +251,10 @@ int run_blocks(evkcu_llm* m, uint32_t B, uint32_t S, bool decode, cudaStream_t s
         LLM_TRY(evkcu_matmul(m->xn, L.wqkv, m->qkv, 1, R, D, m->C, 0, 0, 0, 0, dt, st));
         const uint64_t items = (uint64_t)R * (m->C / 8);
         LLM_TRY(EVKCU_DISPATCH_DTYPE(dt, T, [&] {
-            qkv_rope_append_kernel<T><<<grid_for_items(items), kT, 0, st>>>(
-                (const T*)m->qkv, R, S, 0, decode ? m->d_pos : nullptr, m->Hl, m->Hkvl, m->Dh, c.rope_base,
-                (T*)m->q, decode ? nullptr : (T*)m->kt, decode ? nullptr : (T*)m->vt, (T*)L.kc, (T*)L.vc,
-                c.max_seq);
-            return after_launch("llm qkv_rope_append");
+            return launch_pdl("llm qkv_rope_append", qkv_rope_append_kernel<T>, grid_for_items(items), kT, 0, st,
+                              (const T*)m->qkv, R, S, 0u, decode ? (const uint32_t*)m->d_pos : nullptr, m->Hl,
+                              m->Hkvl, m->Dh, c.rope_base, (T*)m->q, decode ? nullptr : (T*)m->kt,
+                              decode ? nullptr : (T*)m->vt, (T*)L.kc, (T*)L.vc, c.max_seq);
         }));
         if (decode)
             LLM_TRY(evkcu_single_query_attention_devlen(m->q, L.kc, L.vc, m->attn, B, m->Hl, m->Hkvl, m->Dh,
@@ -284,12 +291,12 @@ int head_and_sample(evkcu_llm* m, const void* xrows, uint32_t B, uint32_t* next_
         return EVKCU_OK;
     }
     LLM_TRY(EVKCU_DISPATCH_DTYPE(dt, T, [&] {
-        argmax_key_kernel<T><<<B, 1024, 0, st>>>((const T*)m->logits, m->Vl, c.tp_rank * m->Vl, m->keys);
-        return after_launch("llm argmax_key");
+        return launch_pdl("llm argmax_key", argmax_key_kernel<T>, B, 1024, 0, st, (const T*)m->logits, m->Vl,
+                          c.tp_rank * m->Vl, m->keys);
     }));
     LLM_TRY(nccl_check(ncclAllGather(m->keys, m->keys_all, B, ncclUint64, m->comm, st), "ncclAllGather(keys)"));
-    keys_to_ids_kernel<<<(B + 127) / 128, 128, 0, st>>>(m->keys_all, c.tp_size, B, next_ids);
-    LLM_TRY(after_launch("llm keys_to_ids"));
+    LLM_TRY(launch_pdl("llm keys_to_ids", keys_to_ids_kernel, (B + 127) / 128, 128, 0, st,
+                       (const unsigned long long*)m->keys_all, c.tp_size, B, next_ids));
     if (logits_out) {
         // [t][B][Vl] -> [B][t * Vl]
         LLM_TRY(nccl_check(ncclAllGather(m->logits, m->logits_all, (size_t)B * m->Vl, nccl_type(dt), m->comm, st),
@@ -308,8 +315,7 @@ int decode_body(evkcu_llm* m, const uint32_t* ids, uint32_t* next_ids, void* log
     LLM_TRY(evkcu_embed(m->emb, ids, m->x, c.vocab, c.d_model, B, 4, c.dtype, st));
     LLM_TRY(run_blocks(m, B, 1, true, st));
     LLM_TRY(head_and_sample(m, m->x, B, next_ids, logits_out, st));
-    advance_kernel<<<1, 1, 0, st>>>(m->d_pos, m->d_len);
-    return after_launch("llm advance");
+    return launch_pdl("llm advance", advance_kernel, 1, 1, 0, st, m->d_pos, m->d_len);
 }
 
 std::vector<void*> ws_signature() {

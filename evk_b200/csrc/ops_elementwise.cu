@@ -38,6 +38,8 @@ enum class Unary { Gelu, Scale };
 
 template <typename T, Unary OP>
 __global__ void unary_kernel(const T* __restrict__ in, T* __restrict__ out, uint64_t n, float s) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     uint64_t nvec = n / 8;
     uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -58,6 +60,8 @@ __global__ void unary_kernel(const T* __restrict__ in, T* __restrict__ out, uint
 
 template <typename T>
 __global__ void add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ c, uint64_t n) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     uint64_t nvec = n / 8;
     uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -79,12 +83,16 @@ __global__ void add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* 
 // Scalar fallback for buffers that are not 16-byte aligned.
 template <typename T>
 __global__ void add_scalar_kernel(const T* a, const T* b, T* c, uint64_t n) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += stride)
         c[e] = Elem<T>::from_f(Elem<T>::to_f(a[e]) + Elem<T>::to_f(b[e]));
 }
 template <typename T, Unary OP>
 __global__ void unary_scalar_kernel(const T* in, T* out, uint64_t n, float s) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += stride) {
         float x = Elem<T>::to_f(in[e]);
@@ -95,6 +103,8 @@ __global__ void unary_scalar_kernel(const T* in, T* out, uint64_t n, float s) {
 // shaders/causal_mask.comp:16-33 — row-per-block so each thread only tests j > i.
 template <typename T>
 __global__ void causal_mask_kernel(T* __restrict__ scores, uint64_t rows, uint32_t N) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     const T sentinel = Elem<T>::from_f(-65504.0f);
     for (uint64_t r = blockIdx.x; r < rows; r += gridDim.x) {
         uint32_t i = (uint32_t)(r % N);
@@ -107,6 +117,8 @@ __global__ void causal_mask_kernel(T* __restrict__ scores, uint64_t rows, uint32
 template <typename T, typename I>
 __global__ void embed_kernel(const T* __restrict__ E, const I* __restrict__ idx, T* __restrict__ out,
                              uint32_t vocab, uint32_t dim, uint32_t n_idx, bool vec) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     for (uint32_t r = blockIdx.x; r < n_idx; r += gridDim.x) {
         uint32_t tok = (uint32_t)idx[r];
         if (tok >= vocab) tok = vocab - 1;
@@ -133,10 +145,10 @@ extern "C" int evkcu_add(const void* a, const void* b, void* c, uint64_t n, int 
     bool vec = aligned16(a) && aligned16(b) && aligned16(c);
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
         if (vec)
-            add_kernel<T><<<grid_for(n / 8 + 1), kThreads, 0, as_stream(stream)>>>((const T*)a, (const T*)b, (T*)c, n);
-        else
-            add_scalar_kernel<T><<<grid_for(n), kThreads, 0, as_stream(stream)>>>((const T*)a, (const T*)b, (T*)c, n);
-        return after_launch("evkcu_add");
+            return launch_pdl("evkcu_add", add_kernel<T>, grid_for(n / 8 + 1), kThreads, 0, as_stream(stream),
+                              (const T*)a, (const T*)b, (T*)c, n);
+        return launch_pdl("evkcu_add", add_scalar_kernel<T>, grid_for(n), kThreads, 0, as_stream(stream), (const T*)a,
+                          (const T*)b, (T*)c, n);
     });
 }
 
@@ -147,10 +159,10 @@ static int launch_unary(const void* in, void* out, uint64_t n, float s, int dtyp
     bool vec = aligned16(in) && aligned16(out);
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
         if (vec)
-            unary_kernel<T, OP><<<grid_for(n / 8 + 1), kThreads, 0, as_stream(stream)>>>((const T*)in, (T*)out, n, s);
-        else
-            unary_scalar_kernel<T, OP><<<grid_for(n), kThreads, 0, as_stream(stream)>>>((const T*)in, (T*)out, n, s);
-        return after_launch(name);
+            return launch_pdl(name, unary_kernel<T, OP>, grid_for(n / 8 + 1), kThreads, 0, as_stream(stream),
+                              (const T*)in, (T*)out, n, s);
+        return launch_pdl(name, unary_scalar_kernel<T, OP>, grid_for(n), kThreads, 0, as_stream(stream), (const T*)in,
+                          (T*)out, n, s);
     });
 }
 
@@ -178,8 +190,8 @@ extern "C" int evkcu_causal_mask(void* scores, uint32_t batch, uint32_t N, int d
     DeviceState* s = state();
     unsigned grid = (unsigned)(rows < (uint64_t)s->sm_count * 16 ? rows : (uint64_t)s->sm_count * 16);
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-        causal_mask_kernel<T><<<grid, 256, 0, as_stream(stream)>>>((T*)scores, rows, N);
-        return after_launch("evkcu_causal_mask");
+        return launch_pdl("evkcu_causal_mask", causal_mask_kernel<T>, grid, 256, 0, as_stream(stream), (T*)scores, rows,
+                          N);
     });
 }
 
@@ -195,9 +207,9 @@ extern "C" int evkcu_embed(const void* E, const void* idx, void* out, uint32_t v
     unsigned threads = vec ? (dim / 8 < 128 ? 64 : 128) : 256;
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
         if (idx_bytes == 2)
-            embed_kernel<T, uint16_t><<<grid, threads, 0, as_stream(stream)>>>((const T*)E, (const uint16_t*)idx, (T*)out, vocab, dim, n_idx, vec);
-        else
-            embed_kernel<T, uint32_t><<<grid, threads, 0, as_stream(stream)>>>((const T*)E, (const uint32_t*)idx, (T*)out, vocab, dim, n_idx, vec);
-        return after_launch("evkcu_embed");
+            return launch_pdl("evkcu_embed", embed_kernel<T, uint16_t>, grid, threads, 0, as_stream(stream), (const T*)E,
+                              (const uint16_t*)idx, (T*)out, vocab, dim, n_idx, vec);
+        return launch_pdl("evkcu_embed", embed_kernel<T, uint32_t>, grid, threads, 0, as_stream(stream), (const T*)E,
+                          (const uint32_t*)idx, (T*)out, vocab, dim, n_idx, vec);
     });
 }

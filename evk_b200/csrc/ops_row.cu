@@ -60,6 +60,8 @@ __device__ void block_max_sum(float& m, float& s, float* shm, float* shs) {
 template <typename T, bool VEC>
 __global__ void rms_norm_kernel(const T* __restrict__ in, T* __restrict__ out, const T* __restrict__ gamma,
                                 uint32_t D, float eps) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     __shared__ float sh[32];
     const uint64_t row = blockIdx.x;
     const T* x = in + row * D;
@@ -117,6 +119,8 @@ constexpr float kMaskSentinel = -65504.0f;
 
 template <typename T>
 __global__ void softmax_kernel(const T* __restrict__ in, T* __restrict__ out, uint32_t L, float scale, bool vec) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     __shared__ float shm[32], shs[32];
     const uint64_t row = blockIdx.x;
     const T* x = in + row * L;
@@ -167,6 +171,8 @@ __global__ void softmax_kernel(const T* __restrict__ in, T* __restrict__ out, ui
 template <typename T>
 __global__ void rope_kernel(const T* __restrict__ in, T* __restrict__ out, uint64_t rows, uint32_t seq_len,
                             uint32_t dim, uint32_t head_dim, uint32_t pos_offset, float base, bool vec) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     const uint32_t per_row = vec ? dim / 8 : dim / 2;  // work items per row
     const uint64_t total = rows * per_row;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -225,10 +231,10 @@ extern "C" int evkcu_rms_norm(const void* in, void* out, const void* gamma, uint
     unsigned threads = row_threads(vec ? D / 8 : D);
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
         if (vec)
-            rms_norm_kernel<T, true><<<rows, threads, 0, as_stream(stream)>>>((const T*)in, (T*)out, (const T*)gamma, D, eps);
-        else
-            rms_norm_kernel<T, false><<<rows, threads, 0, as_stream(stream)>>>((const T*)in, (T*)out, (const T*)gamma, D, eps);
-        return after_launch("evkcu_rms_norm");
+            return launch_pdl("evkcu_rms_norm", rms_norm_kernel<T, true>, rows, threads, 0, as_stream(stream),
+                              (const T*)in, (T*)out, (const T*)gamma, D, eps);
+        return launch_pdl("evkcu_rms_norm", rms_norm_kernel<T, false>, rows, threads, 0, as_stream(stream), (const T*)in,
+                          (T*)out, (const T*)gamma, D, eps);
     });
 }
 
@@ -239,8 +245,8 @@ extern "C" int evkcu_softmax(const void* in, void* out, uint32_t rows, uint32_t 
     bool vec = (L % 8 == 0) && aligned16(in) && aligned16(out);
     unsigned threads = row_threads(vec ? L / 8 : L);
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-        softmax_kernel<T><<<rows, threads, 0, as_stream(stream)>>>((const T*)in, (T*)out, L, scale, vec);
-        return after_launch("evkcu_softmax");
+        return launch_pdl("evkcu_softmax", softmax_kernel<T>, rows, threads, 0, as_stream(stream), (const T*)in,
+                          (T*)out, L, scale, vec);
     });
 }
 
@@ -258,8 +264,7 @@ extern "C" int evkcu_rope(const void* in, void* out, uint32_t batch, uint32_t se
     uint64_t want = (items + 255) / 256;
     unsigned grid = (unsigned)(want < (uint64_t)s->sm_count * 8 ? want : (uint64_t)s->sm_count * 8);
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-        rope_kernel<T><<<grid, 256, 0, as_stream(stream)>>>((const T*)in, (T*)out, rows, seq_len, dim, head_dim,
-                                                            pos_offset, base, vec);
-        return after_launch("evkcu_rope");
+        return launch_pdl("evkcu_rope", rope_kernel<T>, grid, 256, 0, as_stream(stream), (const T*)in, (T*)out, rows,
+                          seq_len, dim, head_dim, pos_offset, base, vec);
     });
 }

@@ -55,6 +55,8 @@ __global__ void __launch_bounds__(kThreads) greedy_kernel(const T* __restrict__ 
                                                           uint32_t token_base, uint32_t token_count,
                                                           uint32_t out_bytes, uint64_t* __restrict__ partial,
                                                           unsigned int* __restrict__ tickets) {
+    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
+    pdl_trigger();
     __shared__ uint64_t sh[32];
     __shared__ bool is_last;
     const uint32_t b = blockIdx.y;
@@ -147,9 +149,8 @@ extern "C" int evkcu_greedy_sample(const void* logits, void* out, uint32_t B, ui
     }
     dim3 grid(chunks, B);
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-        greedy_kernel<T><<<grid, kThreads, 0, as_stream(stream)>>>((const T*)logits, out, S, V, position, token_base,
-                                                                  token_count, out_bytes, partial, tickets);
-        return after_launch("evkcu_greedy_sample");
+        return launch_pdl("evkcu_greedy_sample", greedy_kernel<T>, grid, kThreads, 0, as_stream(stream),
+                          (const T*)logits, out, S, V, position, token_base, token_count, out_bytes, partial, tickets);
     });
 }
 
@@ -218,8 +219,7 @@ extern "C" int evkcu_greedy_sample_noalloc(const void* logits, void* out, uint32
     }
     dim3 grid(chunks, B);
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-        greedy_kernel<T><<<grid, kThreads, 0, as_stream(stream)>>>((const T*)logits, out, S, V, position, token_base,
-                                                                  token_count, out_bytes, partial, tickets);
-        return after_launch("evkcu_greedy_sample_noalloc");
+        return launch_pdl("evkcu_greedy_sample_noalloc", greedy_kernel<T>, grid, kThreads, 0, as_stream(stream),
+                          (const T*)logits, out, S, V, position, token_base, token_count, out_bytes, partial, tickets);
     });
 }
