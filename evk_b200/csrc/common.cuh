@@ -158,6 +158,32 @@ __device__ __forceinline__ Vec8 pack8(const float (&f)[8]) {
     return v;
 }
 
+// tanh-approximation GELU, shaders/gelu.comp:15-21.  tanh uses the SFU
+// approximation (max relative error about 2^-11, below the 2-byte output's
+// resolution).
+__device__ __forceinline__ float tanh_fast(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float gelu_f(float x) {
+    const float kAlpha = 0.7978845608028654f;
+    const float kBeta = 0.044715f;
+    float u = kAlpha * (x + kBeta * x * x * x);
+    return 0.5f * x * (1.0f + tanh_fast(u));
+}
+
+// Decode GEMV with a fused epilogue, for the library's own drivers (not part
+// of the C ABI): y[m, :] = f(x[m, :] . W (+ y[m, :])) for Mt <= 16 rows;
+// f = GELU when gelu, else identity; acc adds the existing y (before f).
+// W is [K, N] row-major, or [N, K] with w_kmajor.
+struct GemvEpilogue {
+    int acc = 0;
+    int gelu = 0;
+};
+int gemv_fused(const void* X, const void* W, void* Y, uint32_t Mt, uint32_t K, uint32_t N, bool w_kmajor,
+               GemvEpilogue ep, int dtype, cudaStream_t st);
+
 // --------------------------------------------------------- device limits ----
 // Upper bound, in clock cycles, of any device-side spin wait (~2 s at 2 GHz).
 // A wait that exceeds it records EVKCU_TIMEOUT in the device error word and

@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    T* __restrict__ Y, uint32_t Mt, uint32_t K, uint32_t N, uint32_t ktiles_per_cta, int acc_c,
                    uint32_t idesc, float* __restrict__ partial, unsigned int* __restrict__ tickets,
-                   unsigned int* err) {
+                   unsigned int* err, int gelu) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sW = smem;
@@ -341,6 +341,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
                     if (m < (int)Mt) {
                         float o = v[m];
                         if (acc_c) o += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
+                        if (gelu) o = gelu_f(o);
                         Y[(uint64_t)m * N + n] = Elem<T>::from_f(o);
                     }
                 }
@@ -380,6 +381,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
         }
         if (n < N) {
             if (acc_c) sum += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
+            if (gelu) sum = gelu_f(sum);
             Y[(uint64_t)m * N + n] = Elem<T>::from_f(sum);
         }
     }
@@ -387,7 +389,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
 }
 
 template <typename T, bool W_KMAJOR>
-int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, int acc, int dtype,
+int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, GemvEpilogue ep, int dtype,
                    cudaStream_t st) {
     DeviceState* s = state();
     const uint32_t slabs = (N + GV_COLS - 1) / GV_COLS;
@@ -421,8 +423,8 @@ int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32
     }
     const uint32_t idesc = make_idesc_f16(GV_COLS, GV_MMA_N, dtype == EVKCU_BF16 ? 1 : 0, W_KMAJOR ? 0 : 1, 0);
     dim3 grid(slabs, splits);
-    return launch_pdl("evkcu_matmul(gemv_tc)", kern, grid, GV_THREADS, GV_SMEM, st, mW, mX, Y, Mt, K, N, per, acc, idesc,
-                      partial, tickets, s->d_error);
+    return launch_pdl("evkcu_matmul(gemv_tc)", kern, grid, GV_THREADS, GV_SMEM, st, mW, mX, Y, Mt, K, N, per, ep.acc,
+                      idesc, partial, tickets, s->d_error, ep.gelu);
 }
 
 template <typename T, int BN, bool A_MN, bool B_MN>
@@ -454,11 +456,27 @@ int dispatch_major(bool ta, bool tb, const CUtensorMap& mA, const CUtensorMap& m
 template <typename T>
 int launch_gemv(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, bool tb, int acc, cudaStream_t st) {
     const int dtype = std::is_same<T, __nv_bfloat16>::value ? EVKCU_BF16 : EVKCU_F16;
-    if (tb) return launch_gemv_tc<T, true>(X, W, Y, Mt, K, N, acc, dtype, st);
-    return launch_gemv_tc<T, false>(X, W, Y, Mt, K, N, acc, dtype, st);
+    GemvEpilogue ep;
+    ep.acc = acc;
+    if (tb) return launch_gemv_tc<T, true>(X, W, Y, Mt, K, N, ep, dtype, st);
+    return launch_gemv_tc<T, false>(X, W, Y, Mt, K, N, ep, dtype, st);
 }
 
 }  // namespace
+
+int gemv_fused(const void* X, const void* W, void* Y, uint32_t Mt, uint32_t K, uint32_t N, bool w_kmajor,
+               GemvEpilogue ep, int dtype, cudaStream_t st) {
+    if (Mt == 0 || N == 0) return EVKCU_OK;
+    EVKCU_CHECK_ARG(X && W && Y, EVKCU_BAD_ARG, "gemv_fused: null pointer");
+    EVKCU_CHECK_ARG(Mt <= (uint32_t)kGemvMaxM && K > 0 && K % 8 == 0 && N % 8 == 0, EVKCU_BAD_SHAPE,
+                    "gemv_fused: needs 1..16 rows and K, N multiples of 8");
+    EVKCU_CHECK_ARG(aligned16(X) && aligned16(W) && aligned16(Y), EVKCU_BAD_ALIGN, "gemv_fused: unaligned pointer");
+    return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
+        if (w_kmajor) return launch_gemv_tc<T, true>((const T*)X, (const T*)W, (T*)Y, Mt, K, N, ep, dtype, st);
+        return launch_gemv_tc<T, false>((const T*)X, (const T*)W, (T*)Y, Mt, K, N, ep, dtype, st);
+    });
+}
+
 }  // namespace evkcu
 
 using namespace evkcu;

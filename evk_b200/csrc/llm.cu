@@ -245,6 +245,8 @@ int run_blocks(evkcu_llm* m, uint32_t B, uint32_t S, bool decode, cudaStream_t s
     const evkcu_llm_config& c = m->cfg;
     const uint32_t R = B * S, D = c.d_model;
     const int dt = c.dtype;
+    // Decode rows (<= 16) fold the GELU after W1 into that GEMV.
+    const bool fuse = decode && R <= 16;
     for (uint32_t l = 0; l < c.layers; ++l) {
         LlmLayer& L = m->layers[l];
         LLM_TRY(evkcu_rms_norm(m->x, m->xn, nullptr, R, D, c.eps, dt, st));
@@ -264,8 +266,14 @@ int run_blocks(evkcu_llm* m, uint32_t B, uint32_t S, bool decode, cudaStream_t s
                                           EVKCU_ATTN_CAUSAL, dt, st));
         LLM_TRY(proj_residual(m, m->attn, L.wo, R, m->Hl * m->Dh, st));
         LLM_TRY(evkcu_rms_norm(m->x, m->xn, nullptr, R, D, c.eps, dt, st));
-        LLM_TRY(evkcu_matmul(m->xn, L.w1, m->h1, 1, R, D, m->Fl, 0, 0, 0, 0, dt, st));
-        LLM_TRY(evkcu_gelu(m->h1, m->h1, (uint64_t)R * m->Fl, dt, st));
+        if (fuse) {
+            GemvEpilogue e;
+            e.gelu = 1;
+            LLM_TRY(gemv_fused(m->xn, L.w1, m->h1, R, D, m->Fl, false, e, dt, st));
+        } else {
+            LLM_TRY(evkcu_matmul(m->xn, L.w1, m->h1, 1, R, D, m->Fl, 0, 0, 0, 0, dt, st));
+            LLM_TRY(evkcu_gelu(m->h1, m->h1, (uint64_t)R * m->Fl, dt, st));
+        }
         LLM_TRY(proj_residual(m, m->h1, L.w2, R, m->Fl, st));
     }
     return EVKCU_OK;
@@ -277,11 +285,12 @@ int head_and_sample(evkcu_llm* m, const void* xrows, uint32_t B, uint32_t* next_
     const evkcu_llm_config& c = m->cfg;
     const int dt = c.dtype;
     const uint32_t D = c.d_model;
-    LLM_TRY(evkcu_rms_norm(xrows, m->xn, nullptr, B, D, c.eps, dt, st));
     if (c.tied_embeddings) {
+        LLM_TRY(evkcu_rms_norm(xrows, m->xn, nullptr, B, D, c.eps, dt, st));
         const void* eshard = (const char*)m->emb + (uint64_t)c.tp_rank * m->Vl * D * kE;
         LLM_TRY(evkcu_matmul(m->xn, eshard, m->logits, 1, B, D, m->Vl, 0, 0, 0, EVKCU_MM_TRANSPOSE_B, dt, st));
     } else {
+        LLM_TRY(evkcu_rms_norm(xrows, m->xn, nullptr, B, D, c.eps, dt, st));
         LLM_TRY(evkcu_matmul(m->xn, m->lm_head, m->logits, 1, B, D, m->Vl, 0, 0, 0, 0, dt, st));
     }
     if (c.tp_size == 1) {

@@ -19,21 +19,6 @@ inline unsigned grid_for(uint64_t work_items) {
     return (unsigned)(want < cap ? want : cap);
 }
 
-// tanh-approximation GELU, shaders/gelu.comp:15-21.  tanh uses the SFU
-// approximation (max relative error about 2^-11, below the 2-byte output's
-// resolution).
-__device__ __forceinline__ float tanh_fast(float x) {
-    float y;
-    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
-    return y;
-}
-__device__ __forceinline__ float gelu_f(float x) {
-    const float kAlpha = 0.7978845608028654f;
-    const float kBeta = 0.044715f;
-    float u = kAlpha * (x + kBeta * x * x * x);
-    return 0.5f * x * (1.0f + tanh_fast(u));
-}
-
 enum class Unary { Gelu, Scale };
 
 template <typename T, Unary OP>
