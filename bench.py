@@ -262,11 +262,26 @@ def profile_leg(leg):
         o = torch.empty_like(q)
         for _ in range(5):
             evk.flash_attention(q, k, v, o, heads=H, causal=CAUSAL)
-    else:
+    elif leg == "gemm":
         a, b = (torch.randn(8192, 8192, device="cuda").bfloat16() for _ in range(2))
         c = torch.empty_like(a)
         for _ in range(3):
             evk.matmul(a, b, c)
+    elif leg == "gemv":
+        # C5 decode W1 shape: 16 rows x [4096, 14336] bf16 weight (117 MB)
+        x = torch.randn(16, 4096, device="cuda").bfloat16()
+        w = torch.randn(4096, 14336, device="cuda").bfloat16()
+        y = torch.empty(16, 14336, device="cuda").bfloat16()
+        for _ in range(3):
+            evk.matmul(x, w, y)
+    else:
+        # C4 decode attention: B=8, H=16, Dh=128 over 2048 cached positions (bf16)
+        q = torch.randn(8, 16 * 128, device="cuda").bfloat16()
+        kc = torch.randn(8, 2048, 16 * 128, device="cuda").bfloat16()
+        vc = torch.randn_like(kc)
+        o = torch.empty_like(q)
+        for _ in range(3):
+            evk.single_query_attention(q, kc, vc, o, 16, 2048)
     torch.cuda.synchronize()
     evk.check_device_error()
 
@@ -279,7 +294,7 @@ def main():
     ap.add_argument("--impl", default="evk_b200", choices=["evk_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true")
-    ap.add_argument("--profile-leg", choices=["flash", "gemm"], default=None,
+    ap.add_argument("--profile-leg", choices=["flash", "gemm", "gemv", "decode"], default=None,
                     help="run a few launches of one leg and exit (for ncu captures; prints no JSON)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
