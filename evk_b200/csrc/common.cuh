@@ -173,16 +173,25 @@ __device__ __forceinline__ float gelu_f(float x) {
     return 0.5f * x * (1.0f + tanh_fast(u));
 }
 
-// Decode GEMV with a fused epilogue, for the library's own drivers (not part
-// of the C ABI): y[m, :] = f(x[m, :] . W (+ y[m, :])) for Mt <= 16 rows;
-// f = GELU when gelu, else identity; acc adds the existing y (before f).
-// W is [K, N] row-major, or [N, K] with w_kmajor.
+// Epilogue options of the decode GEMV: acc adds the existing y, gelu applies
+// GELU to the result (after acc).
 struct GemvEpilogue {
     int acc = 0;
     int gelu = 0;
 };
-int gemv_fused(const void* X, const void* W, void* Y, uint32_t Mt, uint32_t K, uint32_t N, bool w_kmajor,
-               GemvEpilogue ep, int dtype, cudaStream_t st);
+
+// evkcu_matmul with an optional GELU applied to each output element (after
+// the optional C +=), for the library's own drivers.
+int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M, uint32_t K, uint32_t N,
+              uint64_t stride_a, uint64_t stride_b, uint64_t stride_c, uint32_t flags, int dtype, int gelu,
+              void* stream);
+
+// evkcu_flash_attention with K and V read at a batch stride of kv_bstride
+// elements (0: N * Hkv * Dh, contiguous), e.g. the first N rows of each
+// sequence's KV cache.  For the library's own drivers.
+int flash_attention_kv_strided(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N,
+                               uint32_t H, uint32_t Hkv, uint32_t Dh, float scale, uint32_t flags, int dtype,
+                               uint64_t kv_bstride, cudaStream_t st);
 
 // --------------------------------------------------------- device limits ----
 // Upper bound, in clock cycles, of any device-side spin wait (~2 s at 2 GHz).

@@ -151,9 +151,14 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
         }
         for (uint32_t t = 0; t < ntiles; ++t) {
             const uint32_t s = t % stages;
-            // Every lane waits; the warp proceeds only if all of them saw the tile.
-            const bool ok = mbar_wait(&full[s], (t / stages) & 1, s_abort, err, kTimeoutDecode);
-            if (!__all_sync(0xffffffffu, ok)) break;
+            // Lane 0 waits (one poller per warp keeps the barrier word from
+            // serialising 256 pollers); the warp follows its outcome.
+            const int ok = __shfl_sync(0xffffffffu,
+                                       lane == 0 ? (int)mbar_wait(&full[s], (t / stages) & 1, s_abort, err,
+                                                                  kTimeoutDecode)
+                                                 : 0,
+                                       0);
+            if (!ok) break;
             const T* kt = reinterpret_cast<const T*>(ring) + (size_t)s * 2 * tile_elems;
             const T* vt = kt + tile_elems;
             const uint32_t r0 = warp * (KPW * STEPS) + grp;   // this lane group's first row

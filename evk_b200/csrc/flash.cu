@@ -503,7 +503,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) flash_simt_kernel(const T* __restrict__ Q, const T* __restrict__ K,
                                                          const T* __restrict__ V, T* __restrict__ O, uint32_t B,
                                                          uint32_t N, uint32_t H, uint32_t Hkv, uint32_t Dh,
-                                                         float scale_log2, int causal) {
+                                                         float scale_log2, int causal, uint64_t kv_bstride) {
     const int lane = threadIdx.x & 31;
     const uint64_t wid = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const uint64_t total = (uint64_t)B * H * N;
@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(256) flash_simt_kernel(const T* __restrict__ Q
     float m = -INFINITY, l = 0.0f;
     const uint32_t kend = causal ? min(N, qi + 1) : N;
     for (uint32_t j = 0; j < kend; ++j) {
-        const T* krow = K + ((uint64_t)b * N + j) * Hkv * Dh + (uint64_t)g * Dh;
+        const T* krow = K + (uint64_t)b * kv_bstride + (uint64_t)j * Hkv * Dh + (uint64_t)g * Dh;
         float s = 0.0f;
         for (uint32_t i = 0; i < per; ++i) {
             uint32_t d = lane + 32 * i;
@@ -537,7 +537,7 @@ __global__ void __launch_bounds__(256) flash_simt_kernel(const T* __restrict__ Q
         float p = ex2(s - mn);
         l = l * a + p;
         m = mn;
-        const T* vrow = V + ((uint64_t)b * N + j) * Hkv * Dh + (uint64_t)g * Dh;
+        const T* vrow = V + (uint64_t)b * kv_bstride + (uint64_t)j * Hkv * Dh + (uint64_t)g * Dh;
         for (uint32_t i = 0; i < per; ++i) {
             uint32_t d = lane + 32 * i;
             float vv = d < Dh ? Elem<T>::to_f(vrow[d]) : 0.0f;
@@ -554,13 +554,15 @@ __global__ void __launch_bounds__(256) flash_simt_kernel(const T* __restrict__ Q
 
 template <typename T, int DH, int NT>
 int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N, uint32_t H,
-                    uint32_t Hkv, float scale_log2, int causal, int dtype, cudaStream_t st) {
+                    uint32_t Hkv, float scale_log2, int causal, int dtype, uint64_t kv_bstride, cudaStream_t st) {
     using Cfg = FlashCfg<DH, NT>;
     CUtensorMap mQ, mK, mV;
     int r;
     if ((r = make_tmap_3d(&mQ, q, (uint64_t)H * DH, N, B, (uint64_t)H * DH, (uint64_t)N * H * DH, 64, FM, dtype))) return r;
-    if ((r = make_tmap_3d(&mK, k, (uint64_t)Hkv * DH, N, B, (uint64_t)Hkv * DH, (uint64_t)N * Hkv * DH, 64, FN, dtype))) return r;
-    if ((r = make_tmap_3d(&mV, v, (uint64_t)Hkv * DH, N, B, (uint64_t)Hkv * DH, (uint64_t)N * Hkv * DH, 64, FN, dtype))) return r;
+    // K/V rows beyond N read as zeros even when the batch stride leaves
+    // memory there (a KV cache): the map's row extent is N.
+    if ((r = make_tmap_3d(&mK, k, (uint64_t)Hkv * DH, N, B, (uint64_t)Hkv * DH, kv_bstride, 64, FN, dtype))) return r;
+    if ((r = make_tmap_3d(&mV, v, (uint64_t)Hkv * DH, N, B, (uint64_t)Hkv * DH, kv_bstride, 64, FN, dtype))) return r;
     auto kern = flash_tc_kernel<T, DH, NT>;
     static bool attr = false;
     if (!attr) {
@@ -583,9 +585,11 @@ int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32
 
 using namespace evkcu;
 
-extern "C" int evkcu_flash_attention(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N,
-                                     uint32_t H, uint32_t Hkv, uint32_t Dh, float scale, uint32_t flags, int dtype,
-                                     void* stream) {
+namespace evkcu {
+
+int flash_attention_kv_strided(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N,
+                               uint32_t H, uint32_t Hkv, uint32_t Dh, float scale, uint32_t flags, int dtype,
+                               uint64_t kv_bstride, cudaStream_t st) {
     if (B == 0 || N == 0 || H == 0) return EVKCU_OK;
     EVKCU_CHECK_ARG(q && k && v && o, EVKCU_BAD_ARG, "evkcu_flash_attention: null pointer");
     EVKCU_CHECK_ARG(dtype == EVKCU_F16 || dtype == EVKCU_BF16, EVKCU_BAD_ARG, "evkcu_flash_attention: unknown dtype");
@@ -594,22 +598,33 @@ extern "C" int evkcu_flash_attention(const void* q, const void* k, const void* v
                     "evkcu_flash_attention: Dh must be a multiple of 16 in [16, 256]");
     EVKCU_CHECK_ARG((uint64_t)B * H <= 0x7fffffffu && (N + FM - 1) / FM <= 65535, EVKCU_BAD_SHAPE,
                     "evkcu_flash_attention: grid too large");
+    if (kv_bstride == 0) kv_bstride = (uint64_t)N * Hkv * Dh;
+    EVKCU_CHECK_ARG(kv_bstride >= (uint64_t)N * Hkv * Dh, EVKCU_BAD_SHAPE,
+                    "evkcu_flash_attention: K/V batch stride smaller than N rows");
     if (!(scale > 0.0f)) scale = 1.0f / sqrtf((float)Dh);
     const float scale_log2 = scale * 1.4426950408889634f;
     const int causal = (flags & EVKCU_ATTN_CAUSAL) ? 1 : 0;
-    cudaStream_t st = as_stream(stream);
-    const bool tma_ok = aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o);
+    const bool tma_ok = aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) && kv_bstride % 8 == 0;
     if (tma_ok && (Dh == 64 || Dh == 128)) {
         return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-            if (Dh == 64) return launch_flash_tc<T, 64, 2>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, st);
-            return launch_flash_tc<T, 128, 1>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, st);
+            if (Dh == 64)
+                return launch_flash_tc<T, 64, 2>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, kv_bstride, st);
+            return launch_flash_tc<T, 128, 1>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, kv_bstride, st);
         });
     }
     const uint64_t warps = (uint64_t)B * H * N;
     const uint64_t blocks = (warps * 32 + 255) / 256;
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
         flash_simt_kernel<T><<<(unsigned)blocks, 256, 0, st>>>((const T*)q, (const T*)k, (const T*)v, (T*)o, B, N, H,
-                                                              Hkv, Dh, scale_log2, causal);
+                                                              Hkv, Dh, scale_log2, causal, kv_bstride);
         return after_launch("evkcu_flash_attention(simt)");
     });
+}
+
+}  // namespace evkcu
+
+extern "C" int evkcu_flash_attention(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N,
+                                     uint32_t H, uint32_t Hkv, uint32_t Dh, float scale, uint32_t flags, int dtype,
+                                     void* stream) {
+    return flash_attention_kv_strided(q, k, v, o, B, N, H, Hkv, Dh, scale, flags, dtype, 0, as_stream(stream));
 }

@@ -50,7 +50,7 @@ template <typename T, int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, T* __restrict__ C,
                    uint32_t M, uint32_t N, uint32_t K, uint64_t strideC, int bcastA, int bcastB, int acc_c,
-                   uint32_t idesc, unsigned int* err) {
+                   uint32_t idesc, unsigned int* err, int gelu) {
     using Cfg = GemmCfg<BN>;
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
@@ -166,6 +166,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 unpack8<T>(*dst, o);
 #pragma unroll
                                 for (int e = 0; e < 8; ++e) f[e] += o[e];
+                            }
+                            if (gelu) {
+#pragma unroll
+                                for (int e = 0; e < 8; ++e) f[e] = gelu_f(f[e]);
                             }
                             *dst = pack8<T>(f);
                         }
@@ -429,7 +433,7 @@ int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32
 
 template <typename T, int BN, bool A_MN, bool B_MN>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch, uint32_t M, uint32_t N, uint32_t K,
-              uint64_t strideC, int bcastA, int bcastB, int acc, int is_bf16, cudaStream_t st) {
+              uint64_t strideC, int bcastA, int bcastB, int acc, int is_bf16, int gelu, cudaStream_t st) {
     using Cfg = GemmCfg<BN>;
     static bool attr_set = false;
     auto kern = gemm_tc_kernel<T, BN, A_MN, B_MN>;
@@ -440,50 +444,41 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
     uint32_t idesc = make_idesc_f16(BM, BN, is_bf16, A_MN, B_MN);
     kern<<<grid, kGemmThreads, Cfg::SMEM, st>>>(ta, tb, C, M, N, K, strideC, bcastA, bcastB, acc, idesc,
-                                                state()->d_error);
+                                                state()->d_error, gelu);
     return after_launch("evkcu_matmul(tcgen05)");
 }
 
 template <typename T, int BN>
 int dispatch_major(bool ta, bool tb, const CUtensorMap& mA, const CUtensorMap& mB, T* C, uint32_t batch, uint32_t M,
-                   uint32_t N, uint32_t K, uint64_t sC, int bA, int bB, int acc, int bf, cudaStream_t st) {
-    if (!ta && !tb) return launch_tc<T, BN, false, true>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, st);
-    if (!ta && tb) return launch_tc<T, BN, false, false>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, st);
-    if (ta && !tb) return launch_tc<T, BN, true, true>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, st);
-    return launch_tc<T, BN, true, false>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, st);
+                   uint32_t N, uint32_t K, uint64_t sC, int bA, int bB, int acc, int bf, int gelu, cudaStream_t st) {
+    if (!ta && !tb) return launch_tc<T, BN, false, true>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
+    if (!ta && tb) return launch_tc<T, BN, false, false>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
+    if (ta && !tb) return launch_tc<T, BN, true, true>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
+    return launch_tc<T, BN, true, false>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
 }
 
 template <typename T>
-int launch_gemv(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, bool tb, int acc, cudaStream_t st) {
+int launch_gemv(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, bool tb, int acc, int gelu,
+                cudaStream_t st) {
     const int dtype = std::is_same<T, __nv_bfloat16>::value ? EVKCU_BF16 : EVKCU_F16;
     GemvEpilogue ep;
     ep.acc = acc;
+    ep.gelu = gelu;
     if (tb) return launch_gemv_tc<T, true>(X, W, Y, Mt, K, N, ep, dtype, st);
     return launch_gemv_tc<T, false>(X, W, Y, Mt, K, N, ep, dtype, st);
 }
 
 }  // namespace
 
-int gemv_fused(const void* X, const void* W, void* Y, uint32_t Mt, uint32_t K, uint32_t N, bool w_kmajor,
-               GemvEpilogue ep, int dtype, cudaStream_t st) {
-    if (Mt == 0 || N == 0) return EVKCU_OK;
-    EVKCU_CHECK_ARG(X && W && Y, EVKCU_BAD_ARG, "gemv_fused: null pointer");
-    EVKCU_CHECK_ARG(Mt <= (uint32_t)kGemvMaxM && K > 0 && K % 8 == 0 && N % 8 == 0, EVKCU_BAD_SHAPE,
-                    "gemv_fused: needs 1..16 rows and K, N multiples of 8");
-    EVKCU_CHECK_ARG(aligned16(X) && aligned16(W) && aligned16(Y), EVKCU_BAD_ALIGN, "gemv_fused: unaligned pointer");
-    return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-        if (w_kmajor) return launch_gemv_tc<T, true>((const T*)X, (const T*)W, (T*)Y, Mt, K, N, ep, dtype, st);
-        return launch_gemv_tc<T, false>((const T*)X, (const T*)W, (T*)Y, Mt, K, N, ep, dtype, st);
-    });
-}
-
 }  // namespace evkcu
 
 using namespace evkcu;
 
-extern "C" int evkcu_matmul(const void* A, const void* B, void* C, uint32_t batch, uint32_t M, uint32_t K, uint32_t N,
-                            uint64_t stride_a, uint64_t stride_b, uint64_t stride_c, uint32_t flags, int dtype,
-                            void* stream) {
+namespace evkcu {
+
+int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M, uint32_t K, uint32_t N,
+              uint64_t stride_a, uint64_t stride_b, uint64_t stride_c, uint32_t flags, int dtype, int gelu,
+              void* stream) {
     if (batch == 0 || M == 0 || N == 0) return EVKCU_OK;
     EVKCU_CHECK_ARG(A && B && C, EVKCU_BAD_ARG, "evkcu_matmul: null pointer");
     EVKCU_CHECK_ARG(dtype == EVKCU_F16 || dtype == EVKCU_BF16, EVKCU_BAD_ARG, "evkcu_matmul: unknown dtype");
@@ -512,7 +507,7 @@ extern "C" int evkcu_matmul(const void* A, const void* B, void* C, uint32_t batc
     const uint64_t Mt = (uint64_t)batch * M;
     if (!ta && Mt <= kGemvMaxM && (batch == 1 || stride_b == 0) && a_contig && c_contig) {
         return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-            return launch_gemv<T>((const T*)A, (const T*)B, (T*)C, (uint32_t)Mt, K, N, tb, acc, st);
+            return launch_gemv<T>((const T*)A, (const T*)B, (T*)C, (uint32_t)Mt, K, N, tb, acc, gelu, st);
         });
     }
 
@@ -543,8 +538,18 @@ extern "C" int evkcu_matmul(const void* A, const void* B, void* C, uint32_t batc
     if (r) return r;
     const uint64_t sC = batch > 1 ? stride_c : 0;
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-        if (BN == 256) return dispatch_major<T, 256>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, st);
-        if (BN == 128) return dispatch_major<T, 128>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, st);
-        return dispatch_major<T, 64>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, st);
+        if (BN == 256)
+            return dispatch_major<T, 256>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
+        if (BN == 128)
+            return dispatch_major<T, 128>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
+        return dispatch_major<T, 64>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
     });
+}
+
+}  // namespace evkcu
+
+extern "C" int evkcu_matmul(const void* A, const void* B, void* C, uint32_t batch, uint32_t M, uint32_t K, uint32_t N,
+                            uint64_t stride_a, uint64_t stride_b, uint64_t stride_c, uint32_t flags, int dtype,
+                            void* stream) {
+    return matmul_ex(A, B, C, batch, M, K, N, stride_a, stride_b, stride_c, flags, dtype, 0, stream);
 }

@@ -68,15 +68,19 @@ __global__ void fill_normal_kernel(T* dst, uint32_t rows, uint32_t cols, uint64_
 // One thread per 8 consecutive elements of a row of qkv [R, (Hq + 2 Hk) * Dh]
 // (q heads, k heads, v heads).  Row r belongs to sequence r / S at position
 // pos0 + r % S (pos0 from *d_pos when given).  q and k are rotated per head
-// (pair p: angle pos * base^(-2p/Dh), as evk::ai::rope with head_dim = Dh);
-// q goes to q_out [R, Hq Dh]; k and v go to the cache [B, max_len, Hk Dh] at
-// their position and, when given, to k_out / v_out [R, Hk Dh].
+// (pair p: angle pos * base^(-2p/Dh), as evk::ai::rope with head_dim = Dh;
+// the Dh/2 inverse frequencies are computed once per block); q goes to
+// q_out [R, Hq Dh]; k and v go to the cache [B, max_len, Hk Dh] at their
+// position.
 template <typename T>
 __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, uint32_t R, uint32_t S, uint32_t pos0,
                                        const uint32_t* __restrict__ d_pos, uint32_t Hq, uint32_t Hk, uint32_t Dh,
-                                       float base, T* __restrict__ q_out, T* __restrict__ k_out,
-                                       T* __restrict__ v_out, T* __restrict__ kcache, T* __restrict__ vcache,
-                                       uint32_t max_len) {
+                                       float base, T* __restrict__ q_out, T* __restrict__ kcache,
+                                       T* __restrict__ vcache, uint32_t max_len) {
+    __shared__ float s_inv_freq[128];  // Dh <= 256
+    for (uint32_t p = threadIdx.x; p < Dh / 2; p += blockDim.x)
+        s_inv_freq[p] = powf(base, -2.0f * (float)p / (float)Dh);
+    __syncthreads();
     pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
     pdl_trigger();
     const uint32_t C = (Hq + 2 * Hk) * Dh;
@@ -96,9 +100,8 @@ __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, uint32_t R, ui
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
                 const uint32_t p = ((c0 % Dh) >> 1) + k;
-                const float inv_freq = powf(base, -2.0f * (float)p / (float)Dh);
                 float sn, cs;
-                sincosf(t * inv_freq, &sn, &cs);
+                sincosf(t * s_inv_freq[p], &sn, &cs);
                 const float x0 = f[2 * k], x1 = f[2 * k + 1];
                 f[2 * k] = x0 * cs - x1 * sn;
                 f[2 * k + 1] = x0 * sn + x1 * cs;
@@ -111,8 +114,6 @@ __global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, uint32_t R, ui
             const uint32_t kc = is_v ? c0 - (Hq + Hk) * Dh : c0 - Hq * Dh;
             const uint64_t crow = ((uint64_t)b * max_len + pos) * Hk * Dh + kc;
             if (pos < max_len) *reinterpret_cast<Vec8*>((is_v ? vcache : kcache) + crow) = v8;
-            T* side = is_v ? v_out : k_out;
-            if (side) *reinterpret_cast<Vec8*>(side + (uint64_t)r * Hk * Dh + kc) = v8;
         }
     }
 }
@@ -191,7 +192,7 @@ struct evkcu_llm {
     void* emb = nullptr;
     void* lm_head = nullptr;  // [D, Vl] when untied
     std::vector<LlmLayer> layers;
-    void *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *kt = nullptr, *vt = nullptr, *attn = nullptr,
+    void *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr,
          *tmp = nullptr, *h1 = nullptr, *xl = nullptr, *logits = nullptr, *logits_all = nullptr;
     unsigned long long *keys = nullptr, *keys_all = nullptr;
     uint32_t *d_pos = nullptr, *d_len = nullptr;
@@ -245,8 +246,6 @@ int run_blocks(evkcu_llm* m, uint32_t B, uint32_t S, bool decode, cudaStream_t s
     const evkcu_llm_config& c = m->cfg;
     const uint32_t R = B * S, D = c.d_model;
     const int dt = c.dtype;
-    // Decode rows (<= 16) fold the GELU after W1 into that GEMV.
-    const bool fuse = decode && R <= 16;
     for (uint32_t l = 0; l < c.layers; ++l) {
         LlmLayer& L = m->layers[l];
         LLM_TRY(evkcu_rms_norm(m->x, m->xn, nullptr, R, D, c.eps, dt, st));
@@ -255,25 +254,20 @@ int run_blocks(evkcu_llm* m, uint32_t B, uint32_t S, bool decode, cudaStream_t s
         LLM_TRY(EVKCU_DISPATCH_DTYPE(dt, T, [&] {
             return launch_pdl("llm qkv_rope_append", qkv_rope_append_kernel<T>, grid_for_items(items), kT, 0, st,
                               (const T*)m->qkv, R, S, 0u, decode ? (const uint32_t*)m->d_pos : nullptr, m->Hl,
-                              m->Hkvl, m->Dh, c.rope_base, (T*)m->q, decode ? nullptr : (T*)m->kt,
-                              decode ? nullptr : (T*)m->vt, (T*)L.kc, (T*)L.vc, c.max_seq);
+                              m->Hkvl, m->Dh, c.rope_base, (T*)m->q, (T*)L.kc, (T*)L.vc, c.max_seq);
         }));
         if (decode)
             LLM_TRY(evkcu_single_query_attention_devlen(m->q, L.kc, L.vc, m->attn, B, m->Hl, m->Hkvl, m->Dh,
                                                          c.max_seq, m->d_len, 0.0f, dt, st));
         else
-            LLM_TRY(evkcu_flash_attention(m->q, m->kt, m->vt, m->attn, B, S, m->Hl, m->Hkvl, m->Dh, 0.0f,
-                                          EVKCU_ATTN_CAUSAL, dt, st));
+            // Prefill attention reads K and V straight from the cache rows
+            // the append kernel just wrote (batch stride max_seq rows).
+            LLM_TRY(flash_attention_kv_strided(m->q, L.kc, L.vc, m->attn, B, S, m->Hl, m->Hkvl, m->Dh, 0.0f,
+                                               EVKCU_ATTN_CAUSAL, dt, (uint64_t)c.max_seq * m->Hkvl * m->Dh, st));
         LLM_TRY(proj_residual(m, m->attn, L.wo, R, m->Hl * m->Dh, st));
         LLM_TRY(evkcu_rms_norm(m->x, m->xn, nullptr, R, D, c.eps, dt, st));
-        if (fuse) {
-            GemvEpilogue e;
-            e.gelu = 1;
-            LLM_TRY(gemv_fused(m->xn, L.w1, m->h1, R, D, m->Fl, false, e, dt, st));
-        } else {
-            LLM_TRY(evkcu_matmul(m->xn, L.w1, m->h1, 1, R, D, m->Fl, 0, 0, 0, 0, dt, st));
-            LLM_TRY(evkcu_gelu(m->h1, m->h1, (uint64_t)R * m->Fl, dt, st));
-        }
+        // W1 with the GELU applied in the GEMM / GEMV epilogue.
+        LLM_TRY(matmul_ex(m->xn, L.w1, m->h1, 1, R, D, m->Fl, 0, 0, 0, 0, dt, 1, st));
         LLM_TRY(proj_residual(m, m->h1, L.w2, R, m->Fl, st));
     }
     return EVKCU_OK;
@@ -410,8 +404,6 @@ extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_l
     A(&m->xn, R * D * kE);
     A(&m->qkv, R * m->C * kE);
     A(&m->q, R * m->Hl * Dh * kE);
-    A(&m->kt, R * m->Hkvl * Dh * kE);
-    A(&m->vt, R * m->Hkvl * Dh * kE);
     A(&m->attn, R * m->Hl * Dh * kE);
     if (t > 1) A(&m->tmp, R * D * kE);
     A(&m->h1, R * m->Fl * kE);
