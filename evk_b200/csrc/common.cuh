@@ -180,6 +180,22 @@ struct GemvEpilogue {
     int gelu = 0;
 };
 
+// Fused argmax of a decode GEMV (greedy sampling of an LM head without a
+// logits round trip).  keys_out[m]: the row's 64-bit greedy key over global
+// indices key_off + n (tensor-parallel shards combine keys); ids_out[m]: the
+// token id (key_off must be 0).  y_out, when not null, also receives the
+// logits.  Scratch pointers are filled in by the launcher.
+struct GemvArgmax {
+    unsigned long long* slab_keys = nullptr;
+    unsigned int* ticket = nullptr;
+    unsigned long long* keys_out = nullptr;
+    uint32_t* ids_out = nullptr;
+    uint32_t key_off = 0;
+    int write_y = 1;
+};
+int gemv_argmax(const void* X, const void* W, uint32_t Mt, uint32_t K, uint32_t N, bool w_kmajor, uint32_t key_off,
+                unsigned long long* keys_out, uint32_t* ids_out, void* y_out, int dtype, cudaStream_t st);
+
 // evkcu_matmul with an optional GELU applied to each output element (after
 // the optional C +=), for the library's own drivers.
 int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M, uint32_t K, uint32_t N,

@@ -25,6 +25,7 @@
 #include <string>
 #include <type_traits>
 
+#include "greedy_key.cuh"
 #include "sm100.cuh"
 
 namespace evkcu {
@@ -214,12 +215,18 @@ constexpr int GV_SMEM = GV_STAGES * GV_STAGE_BYTES + 1024 + 256;
 constexpr int GV_THREADS = 192;
 constexpr uint32_t kTimeoutGemv = 0x301;
 
+template <typename T>
+__device__ void gemv_argmax_tail(const float* s_val, uint32_t Mt, uint32_t N, uint32_t n0, const GemvArgmax& am);
+template <typename T>
+__device__ void gemv_combine_splits(const float* __restrict__ partial, T* __restrict__ Y, uint32_t Mt, uint32_t N,
+                                    uint32_t n0, int acc_c, int gelu, int write_y, float* s_val);
+
 template <typename T, bool W_KMAJOR>
 __global__ void __launch_bounds__(GV_THREADS, 2)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    T* __restrict__ Y, uint32_t Mt, uint32_t K, uint32_t N, uint32_t ktiles_per_cta, int acc_c,
                    uint32_t idesc, float* __restrict__ partial, unsigned int* __restrict__ tickets,
-                   unsigned int* err, int gelu) {
+                   unsigned int* err, int gelu, GemvArgmax am) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sW = smem;
@@ -339,15 +346,20 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
         tc_fence_before();
         if (have && gridDim.y == 1) {
             const uint32_t n = n0 + nn;
-            if (n < N) {
+            // With an argmax the TMA ring (idle now) stages the stored values.
+            float* s_val = reinterpret_cast<float*>(smem);  // [GV_MMA_N][GV_COLS]
 #pragma unroll
-                for (int m = 0; m < GV_MMA_N; ++m) {
-                    if (m < (int)Mt) {
-                        float o = v[m];
+            for (int m = 0; m < GV_MMA_N; ++m) {
+                if (m < (int)Mt) {
+                    float o = v[m];
+                    if (n < N) {
                         if (acc_c) o += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
                         if (gelu) o = gelu_f(o);
-                        Y[(uint64_t)m * N + n] = Elem<T>::from_f(o);
+                        const T st = Elem<T>::from_f(o);
+                        if (am.write_y) Y[(uint64_t)m * N + n] = st;
+                        o = Elem<T>::to_f(st);
                     }
+                    if (am.slab_keys) s_val[m * GV_COLS + nn] = o;
                 }
             }
         } else if (have) {
@@ -363,11 +375,77 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
         tc_fence_after();
         tmem_dealloc(tmem, 32);
     }
-    if (gridDim.y == 1 || *s_abort) return;
-    if (threadIdx.x == 0) is_last = atomicAdd(&tickets[blockIdx.x], 1u) == gridDim.y - 1;
-    __syncthreads();
-    if (!is_last) return;
+    if (*s_abort) return;
+    if (gridDim.y > 1) {
+        if (threadIdx.x == 0) is_last = atomicAdd(&tickets[blockIdx.x], 1u) == gridDim.y - 1;
+        __syncthreads();
+        if (!is_last) return;
+        __threadfence();
+        gemv_combine_splits<T>(partial, Y, Mt, N, n0, acc_c, gelu, am.write_y,
+                               am.slab_keys ? reinterpret_cast<float*>(smem) : nullptr);
+        if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
+    }
+    if (am.slab_keys) gemv_argmax_tail<T>(reinterpret_cast<const float*>(smem), Mt, N, n0, am);
+}
+
+// Fused argmax over the GEMV's outputs (greedy sampling of an LM head): each
+// slab reduces its staged values (already rounded to the storage type, i.e.
+// the logits a separate kernel would read) to one 64-bit selection key per
+// row (greedy_key.cuh: the reference's tie rule), and the last slab to finish
+// (global ticket) reduces the slab keys to the row's key or token id.
+// Maxima of keys are exact, so the result is independent of the order.
+template <typename T>
+__device__ void gemv_argmax_tail(const float* s_val, uint32_t Mt, uint32_t N, uint32_t n0, const GemvArgmax& am) {
+    __shared__ bool last_slab;
+    __syncthreads();  // s_val complete
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nwarps = blockDim.x >> 5;
+    for (uint32_t m = warp; m < Mt; m += nwarps) {
+        unsigned long long best = 0ull;
+#pragma unroll
+        for (int e = 0; e < GV_COLS / 32; ++e) {
+            const uint32_t c = lane + 32 * e;
+            const uint32_t n = n0 + c;
+            const unsigned long long k = n < N ? elem_key(s_val[m * GV_COLS + c], am.key_off + n) : 0ull;
+            best = k > best ? k : best;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+            best = t > best ? t : best;
+        }
+        if (lane == 0) am.slab_keys[(uint64_t)blockIdx.x * GV_MMA_N + m] = best;
+    }
     __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last_slab = atomicAdd(am.ticket, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last_slab) return;
+    __threadfence();
+    for (uint32_t m = warp; m < Mt; m += nwarps) {
+        unsigned long long best = 0ull;
+        for (uint32_t sl = lane; sl < gridDim.x; sl += 32) {
+            const unsigned long long k = __ldcg(am.slab_keys + (uint64_t)sl * GV_MMA_N + m);
+            best = k > best ? k : best;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+            best = t > best ? t : best;
+        }
+        if (lane == 0) {
+            if (am.keys_out) am.keys_out[m] = best;
+            if (am.ids_out) am.ids_out[m] = best ? key_to_offset(best) : 0u;
+        }
+    }
+    if (threadIdx.x == 0) *am.ticket = 0u;
+}
+
+// Last CTA of a slab: adds the split partials in split order and applies
+// the epilogue; optionally stages the stored values for the argmax.
+template <typename T>
+__device__ void gemv_combine_splits(const float* __restrict__ partial, T* __restrict__ Y, uint32_t Mt, uint32_t N,
+                                    uint32_t n0, int acc_c, int gelu, int write_y, float* s_val) {
     const float* base = partial + (uint64_t)blockIdx.x * gridDim.y * (GV_MMA_N * GV_COLS);
     for (uint32_t i = threadIdx.x; i < Mt * GV_COLS; i += blockDim.x) {
         const uint32_t m = i / GV_COLS, c = i % GV_COLS, n = n0 + c;
@@ -386,15 +464,17 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
         if (n < N) {
             if (acc_c) sum += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
             if (gelu) sum = gelu_f(sum);
-            Y[(uint64_t)m * N + n] = Elem<T>::from_f(sum);
+            const T st = Elem<T>::from_f(sum);
+            if (write_y) Y[(uint64_t)m * N + n] = st;
+            sum = Elem<T>::to_f(st);
         }
+        if (s_val) s_val[m * GV_COLS + c] = sum;
     }
-    if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
 }
 
 template <typename T, bool W_KMAJOR>
 int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, GemvEpilogue ep, int dtype,
-                   cudaStream_t st) {
+                   cudaStream_t st, GemvArgmax am = GemvArgmax()) {
     DeviceState* s = state();
     const uint32_t slabs = (N + GV_COLS - 1) / GV_COLS;
     const uint32_t ktiles = (K + GV_BK - 1) / GV_BK;
@@ -411,13 +491,21 @@ int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32
     if (r) return r;
     float* partial = nullptr;
     unsigned int* tickets = nullptr;
-    if (splits > 1) {
-        if (slabs > kMaxTickets) return fail(EVKCU_BAD_SHAPE, "evkcu_matmul: N too large for the GEMV path");
-        const size_t pbytes = (size_t)slabs * splits * GV_MMA_N * GV_COLS * sizeof(float);
-        char* ws = (char*)workspace(WS_GEMV, kTicketBytes + pbytes);
+    const bool argmax = am.keys_out || am.ids_out;
+    if (splits > 1 || argmax) {
+        // Scratch: slab tickets (the last one is the argmax's global ticket),
+        // split partials, then the argmax's per-slab keys.
+        if (slabs >= kMaxTickets) return fail(EVKCU_BAD_SHAPE, "evkcu_matmul: N too large for the GEMV path");
+        const size_t pbytes = splits > 1 ? (size_t)slabs * splits * GV_MMA_N * GV_COLS * sizeof(float) : 0;
+        const size_t kbytes = argmax ? (size_t)slabs * GV_MMA_N * sizeof(unsigned long long) : 0;
+        char* ws = (char*)workspace(WS_GEMV, kTicketBytes + pbytes + kbytes);
         if (!ws) return fail(EVKCU_CUDA_ERROR, "evkcu_matmul: workspace allocation failed");
         tickets = (unsigned int*)ws;
         partial = (float*)(ws + kTicketBytes);
+        if (argmax) {
+            am.ticket = tickets + (kMaxTickets - 1);
+            am.slab_keys = (unsigned long long*)(ws + kTicketBytes + pbytes);
+        }
     }
     auto kern = gemv_tc_kernel<T, W_KMAJOR>;
     static bool attr_set = false;
@@ -428,7 +516,7 @@ int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32
     const uint32_t idesc = make_idesc_f16(GV_COLS, GV_MMA_N, dtype == EVKCU_BF16 ? 1 : 0, W_KMAJOR ? 0 : 1, 0);
     dim3 grid(slabs, splits);
     return launch_pdl("evkcu_matmul(gemv_tc)", kern, grid, GV_THREADS, GV_SMEM, st, mW, mX, Y, Mt, K, N, per, ep.acc,
-                      idesc, partial, tickets, s->d_error, ep.gelu);
+                      idesc, partial, tickets, s->d_error, ep.gelu, am);
 }
 
 template <typename T, int BN, bool A_MN, bool B_MN>
@@ -543,6 +631,27 @@ int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M,
         if (BN == 128)
             return dispatch_major<T, 128>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
         return dispatch_major<T, 64>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
+    });
+}
+
+int gemv_argmax(const void* X, const void* W, uint32_t Mt, uint32_t K, uint32_t N, bool w_kmajor, uint32_t key_off,
+                unsigned long long* keys_out, uint32_t* ids_out, void* y_out, int dtype, cudaStream_t st) {
+    if (Mt == 0) return EVKCU_OK;
+    EVKCU_CHECK_ARG(X && W && (keys_out || ids_out), EVKCU_BAD_ARG, "gemv_argmax: null pointer");
+    EVKCU_CHECK_ARG(Mt <= (uint32_t)kGemvMaxM && K > 0 && K % 8 == 0 && N > 0 && N % 8 == 0, EVKCU_BAD_SHAPE,
+                    "gemv_argmax: needs 1..16 rows and K, N multiples of 8");
+    EVKCU_CHECK_ARG(aligned16(X) && aligned16(W) && (!y_out || aligned16(y_out)), EVKCU_BAD_ALIGN,
+                    "gemv_argmax: unaligned pointer");
+    GemvArgmax am;
+    am.keys_out = keys_out;
+    am.ids_out = ids_out;
+    am.key_off = key_off;
+    am.write_y = y_out ? 1 : 0;
+    return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
+        GemvEpilogue ep;
+        if (w_kmajor)
+            return launch_gemv_tc<T, true>((const T*)X, (const T*)W, (T*)y_out, Mt, K, N, ep, dtype, st, am);
+        return launch_gemv_tc<T, false>((const T*)X, (const T*)W, (T*)y_out, Mt, K, N, ep, dtype, st, am);
     });
 }
 

@@ -279,7 +279,21 @@ int head_and_sample(evkcu_llm* m, const void* xrows, uint32_t B, uint32_t* next_
     const evkcu_llm_config& c = m->cfg;
     const int dt = c.dtype;
     const uint32_t D = c.d_model;
-    if (c.tied_embeddings) {
+    const bool tied = c.tied_embeddings;
+    const void* w_head = tied ? (const void*)((const char*)m->emb + (uint64_t)c.tp_rank * m->Vl * D * kE) : m->lm_head;
+    if (B <= 16 && !logits_out) {
+        // Fused LM head + greedy argmax: the GEMV reduces its own outputs to
+        // selection keys, so the [B, V] logits never reach HBM.
+        LLM_TRY(evkcu_rms_norm(xrows, m->xn, nullptr, B, D, c.eps, dt, st));
+        if (c.tp_size == 1)
+            return gemv_argmax(m->xn, w_head, B, D, m->Vl, tied, 0, nullptr, next_ids, nullptr, dt, st);
+        LLM_TRY(gemv_argmax(m->xn, w_head, B, D, m->Vl, tied, c.tp_rank * m->Vl, (unsigned long long*)m->keys,
+                            nullptr, nullptr, dt, st));
+        LLM_TRY(nccl_check(ncclAllGather(m->keys, m->keys_all, B, ncclUint64, m->comm, st), "ncclAllGather(keys)"));
+        return launch_pdl("llm keys_to_ids", keys_to_ids_kernel, (B + 127) / 128, 128, 0, st,
+                          (const unsigned long long*)m->keys_all, c.tp_size, B, next_ids);
+    }
+    if (tied) {
         LLM_TRY(evkcu_rms_norm(xrows, m->xn, nullptr, B, D, c.eps, dt, st));
         const void* eshard = (const char*)m->emb + (uint64_t)c.tp_rank * m->Vl * D * kE;
         LLM_TRY(evkcu_matmul(m->xn, eshard, m->logits, 1, B, D, m->Vl, 0, 0, 0, EVKCU_MM_TRANSPOSE_B, dt, st));

@@ -128,3 +128,36 @@ def test_llm_random_init_is_deterministic():
         outs.append(lg.clone())
         m.close()
     assert torch.equal(outs[0], outs[1])
+
+
+@pytest.mark.parametrize("tied", [True, False])
+def test_llm_fused_head_argmax_matches_logits_path(tied):
+    """Without logits the LM-head GEMV reduces its outputs to greedy keys
+    (fused argmax); the ids must equal those of the logits + greedy_sample
+    path bit for bit, prefill and decode."""
+    import evk_b200
+
+    evk_b200.init(0)
+    V = 4000  # 32 slabs of 128 columns, a ragged last one
+    runs = []
+    for with_logits in (True, False):
+        m = evk_b200.Llm(2, 256, 4, 512, V, 3, 48, dtype=1, tied_embeddings=tied)
+        m.init_random(seed=21, std=0.05)
+        tok = torch.from_numpy(np.random.default_rng(4).integers(0, V, size=(3, 20)).astype(np.int32)).cuda()
+        nxt = torch.zeros(3, dtype=torch.int32, device="cuda")
+        stream = torch.cuda.Stream()
+        ids = []
+        with torch.cuda.stream(stream):
+            lg = torch.empty(3, V, dtype=torch.bfloat16, device="cuda") if with_logits else None
+            m.prefill(tok, nxt, lg, stream=stream)
+            ids.append(nxt.clone())
+            cur = nxt.clone()
+            for _ in range(5):
+                out = torch.zeros(3, dtype=torch.int32, device="cuda")
+                m.decode(cur, out, lg, stream=stream)
+                ids.append(out)
+                cur = out
+        torch.cuda.synchronize()
+        runs.append(torch.stack(ids).cpu().numpy())
+        m.close()
+    assert np.array_equal(runs[0], runs[1]), (runs[0], runs[1])
