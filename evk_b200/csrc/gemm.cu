@@ -446,29 +446,45 @@ __device__ void gemv_argmax_tail(const float* s_val, uint32_t Mt, uint32_t N, ui
 template <typename T>
 __device__ void gemv_combine_splits(const float* __restrict__ partial, T* __restrict__ Y, uint32_t Mt, uint32_t N,
                                     uint32_t n0, int acc_c, int gelu, int write_y, float* s_val) {
+    // Thread g takes 4 consecutive outputs (one float4 of every split's
+    // partial) and keeps up to 16 splits' loads in flight before adding them
+    // in split order, so the combine costs a few L2 round trips, not one per
+    // split.
     const float* base = partial + (uint64_t)blockIdx.x * gridDim.y * (GV_MMA_N * GV_COLS);
-    for (uint32_t i = threadIdx.x; i < Mt * GV_COLS; i += blockDim.x) {
-        const uint32_t m = i / GV_COLS, c = i % GV_COLS, n = n0 + c;
-        // Partials are read from L2 (.cg: written by other CTAs) eight at a
-        // time, then added in split order.
-        float sum = 0.0f;
-        for (uint32_t y0 = 0; y0 < gridDim.y; y0 += 8) {
-            float t[8];
+    const uint32_t groups = Mt * GV_COLS / 4;
+    for (uint32_t g = threadIdx.x; g < groups; g += blockDim.x) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (uint32_t y0 = 0; y0 < gridDim.y; y0 += 16) {
+            float4 t[16];
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                t[j] = y0 + j < gridDim.y ? __ldcg(base + (uint64_t)(y0 + j) * (GV_MMA_N * GV_COLS) + i) : 0.0f;
+            for (int j = 0; j < 16; ++j)
+                if (y0 + j < gridDim.y)
+                    t[j] = __ldcg(reinterpret_cast<const float4*>(base + (uint64_t)(y0 + j) * (GV_MMA_N * GV_COLS)) + g);
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (y0 + j < gridDim.y) sum += t[j];
+            for (int j = 0; j < 16; ++j) {
+                if (y0 + j < gridDim.y) {
+                    acc.x += t[j].x;
+                    acc.y += t[j].y;
+                    acc.z += t[j].z;
+                    acc.w += t[j].w;
+                }
+            }
         }
-        if (n < N) {
-            if (acc_c) sum += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
-            if (gelu) sum = gelu_f(sum);
-            const T st = Elem<T>::from_f(sum);
-            if (write_y) Y[(uint64_t)m * N + n] = st;
-            sum = Elem<T>::to_f(st);
+        const float sums[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const uint32_t i = g * 4 + e;
+            const uint32_t m = i / GV_COLS, c = i % GV_COLS, n = n0 + c;
+            float sum = sums[e];
+            if (n < N) {
+                if (acc_c) sum += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
+                if (gelu) sum = gelu_f(sum);
+                const T st = Elem<T>::from_f(sum);
+                if (write_y) Y[(uint64_t)m * N + n] = st;
+                sum = Elem<T>::to_f(st);
+            }
+            if (s_val) s_val[m * GV_COLS + c] = sum;
         }
-        if (s_val) s_val[m * GV_COLS + c] = sum;
     }
 }
 
@@ -478,9 +494,15 @@ int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32
     DeviceState* s = state();
     const uint32_t slabs = (N + GV_COLS - 1) / GV_COLS;
     const uint32_t ktiles = (K + GV_BK - 1) / GV_BK;
-    // One resident wave: two CTAs per SM, whole k-tiles per split.
-    const uint32_t slots = 2 * (uint32_t)s->sm_count;
-    uint32_t splits = std::max<uint32_t>(1, std::min<uint32_t>(ktiles, slots / slabs));
+    // Weights under 64 MB: one CTA per SM (a 6-deep ring each keeps ~16 MB
+    // of loads in flight), leaving the SM's other slot to the next kernel of
+    // a decode chain, which (programmatic dependent launch) streams its own
+    // weights meanwhile.  Larger weights: two CTAs per SM.  Whole k-tiles per
+    // split, at least 4 where K allows (each split adds a partial to the
+    // combine).
+    const uint32_t per_sm = (uint64_t)K * N * sizeof(T) < (64ull << 20) ? 1u : 2u;
+    const uint32_t slots = per_sm * (uint32_t)s->sm_count;
+    uint32_t splits = std::max<uint32_t>(1, std::min<uint32_t>(std::max<uint32_t>(1, ktiles / 4), slots / slabs));
     const uint32_t per = (ktiles + splits - 1) / splits;
     splits = (ktiles + per - 1) / per;
     CUtensorMap mW, mX;

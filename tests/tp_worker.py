@@ -36,6 +36,26 @@ def run(model, tokens, steps, V, tdt):
     return torch.stack(logits), torch.stack(ids)
 
 
+def run_ids(model, tokens, steps):
+    """Without logits: fused LM-head argmax (rank keys + all-gather), decode
+    steps replayed as CUDA graphs."""
+    B = tokens.shape[0]
+    stream = torch.cuda.Stream()
+    ids = []
+    with torch.cuda.stream(stream):
+        nxt = torch.zeros(B, dtype=torch.int32, device="cuda")
+        model.prefill(tokens, nxt, stream=stream)
+        ids.append(nxt.clone())
+        cur = nxt.clone()
+        for _ in range(steps):
+            out = torch.zeros(B, dtype=torch.int32, device="cuda")
+            model.decode(cur, out, stream=stream)
+            ids.append(out)
+            cur = out
+    torch.cuda.synchronize()
+    return torch.stack(ids).cpu()
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
@@ -54,6 +74,12 @@ def main():
         tp.init_random(seed=77, std=0.02)
         lt, it = run(tp, tokens, 6, CFG["vocab"], tdt)
         tp.close()
+        # Same model again without logits: the fused head must pick the same ids.
+        tp = ev.Llm(**CFG, dtype=dtype, tied_embeddings=tied, tp_rank=rank, tp_size=world, comm=comm)
+        tp.init_random(seed=77, std=0.02)
+        it_fused = run_ids(tp, tokens, 6)
+        tp.close()
+        assert torch.equal(it_fused, it), (it_fused, it)
         if rank == 0:
             one = ev.Llm(**CFG, dtype=dtype, tied_embeddings=tied)
             one.init_random(seed=77, std=0.02)
