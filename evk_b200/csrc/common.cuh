@@ -196,6 +196,23 @@ struct GemvArgmax {
 int gemv_argmax(const void* X, const void* W, uint32_t Mt, uint32_t K, uint32_t N, bool w_kmajor, uint32_t key_off,
                 unsigned long long* keys_out, uint32_t* ids_out, void* y_out, int dtype, cudaStream_t st);
 
+// Row-parallel decode GEMV fused with the tensor-parallel all-reduce and the
+// residual add: y[m, :] += sum over ranks of (x_r[m, :] . W_r).  Each slab's
+// final fp32 partial is pushed into every rank's buf (plain stores over
+// NVLink peer mappings), a per-slab flag carrying *epoch is published to
+// every rank, and after a bounded wait for all ranks' flags each rank sums
+// the partials in rank order (identical on every rank) and adds them to y.
+// buf[q]: rank q's [2][tp][16][N] fp32 (double-buffered by call-site
+// parity); flags[q]: rank q's [call sites][slabs][tp] words.
+struct GemvAllReduce {
+    float* buf[8] = {};
+    uint32_t* flags[8] = {};
+    const uint32_t* epoch = nullptr;
+    uint32_t tp = 0, rank = 0, callsite = 0;
+};
+int gemv_allreduce_residual(const void* X, const void* W, void* Y, uint32_t Mt, uint32_t K, uint32_t N,
+                            const GemvAllReduce& ar, int dtype, cudaStream_t st);
+
 // evkcu_matmul with an optional GELU applied to each output element (after
 // the optional C +=), for the library's own drivers.
 int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M, uint32_t K, uint32_t N,

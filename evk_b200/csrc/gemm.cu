@@ -219,14 +219,17 @@ template <typename T>
 __device__ void gemv_argmax_tail(const float* s_val, uint32_t Mt, uint32_t N, uint32_t n0, const GemvArgmax& am);
 template <typename T>
 __device__ void gemv_combine_splits(const float* __restrict__ partial, T* __restrict__ Y, uint32_t Mt, uint32_t N,
-                                    uint32_t n0, int acc_c, int gelu, int write_y, float* s_val);
+                                    uint32_t n0, int acc_c, int gelu, int write_y, float* s_val, bool raw);
+template <typename T>
+__device__ void gemv_allreduce_tail(const float* s_val, T* __restrict__ Y, uint32_t Mt, uint32_t N, uint32_t n0,
+                                    const GemvAllReduce& ar, unsigned int* err);
 
 template <typename T, bool W_KMAJOR>
 __global__ void __launch_bounds__(GV_THREADS, 2)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    T* __restrict__ Y, uint32_t Mt, uint32_t K, uint32_t N, uint32_t ktiles_per_cta, int acc_c,
                    uint32_t idesc, float* __restrict__ partial, unsigned int* __restrict__ tickets,
-                   unsigned int* err, int gelu, GemvArgmax am) {
+                   unsigned int* err, int gelu, GemvArgmax am, GemvAllReduce ar) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sW = smem;
@@ -360,6 +363,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
                         o = Elem<T>::to_f(st);
                     }
                     if (am.slab_keys) s_val[m * GV_COLS + nn] = o;
+                    if (ar.tp) s_val[m * GV_COLS + nn] = v[m];
                 }
             }
         } else if (have) {
@@ -382,10 +386,83 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
         if (!is_last) return;
         __threadfence();
         gemv_combine_splits<T>(partial, Y, Mt, N, n0, acc_c, gelu, am.write_y,
-                               am.slab_keys ? reinterpret_cast<float*>(smem) : nullptr);
+                               (am.slab_keys || ar.tp) ? reinterpret_cast<float*>(smem) : nullptr, ar.tp != 0);
         if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
     }
     if (am.slab_keys) gemv_argmax_tail<T>(reinterpret_cast<const float*>(smem), Mt, N, n0, am);
+    if (ar.tp) gemv_allreduce_tail<T>(reinterpret_cast<const float*>(smem), Y, Mt, N, n0, ar, err);
+}
+
+// Tensor-parallel all-reduce of one slab's fp32 partial (see GemvAllReduce):
+// push to every rank, publish the flag, wait (bounded) for every rank's flag,
+// sum in rank order, add to the residual y.
+template <typename T>
+__device__ void gemv_allreduce_tail(const float* s_val, T* __restrict__ Y, uint32_t Mt, uint32_t N, uint32_t n0,
+                                    const GemvAllReduce& ar, unsigned int* err) {
+    __shared__ int s_ok;
+    __syncthreads();  // s_val complete
+    const uint32_t slab = blockIdx.x, slabs = gridDim.x;
+    const uint32_t par = ar.callsite & 1;
+    const uint32_t ep = *ar.epoch;
+    const uint32_t groups = Mt * GV_COLS / 4;
+    // 1. This rank's partial into slot [par][rank] of every rank's buffer.
+    for (uint32_t g = threadIdx.x; g < groups; g += blockDim.x) {
+        const uint32_t m = (g * 4) / GV_COLS, c = (g * 4) % GV_COLS;
+        const float4 v = *reinterpret_cast<const float4*>(s_val + m * GV_COLS + c);
+        const uint64_t off = ((uint64_t)(par * ar.tp + ar.rank) * GV_MMA_N + m) * N + n0 + c;
+        for (uint32_t q = 0; q < ar.tp; ++q)
+            if (n0 + c < N) *reinterpret_cast<float4*>(ar.buf[q] + off) = v;
+    }
+    __threadfence_system();
+    __syncthreads();
+    const uint64_t fslot = ((uint64_t)ar.callsite * slabs + slab) * ar.tp;
+    if (threadIdx.x == 0) {
+        for (uint32_t q = 0; q < ar.tp; ++q)
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ar.flags[q] + fslot + ar.rank), "r"(ep)
+                         : "memory");
+        // 2. Every rank's partial has landed here once its flag shows ep.
+        int ok = 1;
+        const long long t0 = clock64();
+        for (uint32_t q = 0; q < ar.tp && ok; ++q) {
+            uint32_t f;
+            while (true) {
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(ar.flags[ar.rank] + fslot + q)
+                             : "memory");
+                if (f == ep) break;
+                if (clock64() - t0 > kSpinLimitCycles / 2 || *reinterpret_cast<volatile unsigned int*>(err)) {
+                    atomicCAS(err, 0u, 0x302u);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(20);
+            }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    __threadfence();
+    // 3. Sum in rank order (the same on every rank) and add to the residual.
+    const float* mine = ar.buf[ar.rank];
+    for (uint32_t g = threadIdx.x; g < groups; g += blockDim.x) {
+        const uint32_t m = (g * 4) / GV_COLS, c = (g * 4) % GV_COLS, n = n0 + c;
+        if (n >= N) continue;
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (uint32_t q = 0; q < ar.tp; ++q) {
+            const float4 v = __ldcv(reinterpret_cast<const float4*>(
+                mine + ((uint64_t)(par * ar.tp + q) * GV_MMA_N + m) * N + n));
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const float a[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            T* y = Y + (uint64_t)m * N + n + e;
+            *y = Elem<T>::from_f(Elem<T>::to_f(*y) + a[e]);
+        }
+    }
 }
 
 // Fused argmax over the GEMV's outputs (greedy sampling of an LM head): each
@@ -445,7 +522,7 @@ __device__ void gemv_argmax_tail(const float* s_val, uint32_t Mt, uint32_t N, ui
 // the epilogue; optionally stages the stored values for the argmax.
 template <typename T>
 __device__ void gemv_combine_splits(const float* __restrict__ partial, T* __restrict__ Y, uint32_t Mt, uint32_t N,
-                                    uint32_t n0, int acc_c, int gelu, int write_y, float* s_val) {
+                                    uint32_t n0, int acc_c, int gelu, int write_y, float* s_val, bool raw) {
     // Thread g takes 4 consecutive outputs (one float4 of every split's
     // partial) and keeps up to 16 splits' loads in flight before adding them
     // in split order, so the combine costs a few L2 round trips, not one per
@@ -476,6 +553,10 @@ __device__ void gemv_combine_splits(const float* __restrict__ partial, T* __rest
             const uint32_t i = g * 4 + e;
             const uint32_t m = i / GV_COLS, c = i % GV_COLS, n = n0 + c;
             float sum = sums[e];
+            if (raw) {  // the unrounded fp32 sum, for the all-reduce
+                s_val[m * GV_COLS + c] = sum;
+                continue;
+            }
             if (n < N) {
                 if (acc_c) sum += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
                 if (gelu) sum = gelu_f(sum);
@@ -490,7 +571,7 @@ __device__ void gemv_combine_splits(const float* __restrict__ partial, T* __rest
 
 template <typename T, bool W_KMAJOR>
 int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, GemvEpilogue ep, int dtype,
-                   cudaStream_t st, GemvArgmax am = GemvArgmax()) {
+                   cudaStream_t st, GemvArgmax am = GemvArgmax(), const GemvAllReduce& ar = GemvAllReduce()) {
     DeviceState* s = state();
     const uint32_t slabs = (N + GV_COLS - 1) / GV_COLS;
     const uint32_t ktiles = (K + GV_BK - 1) / GV_BK;
@@ -538,7 +619,7 @@ int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32
     const uint32_t idesc = make_idesc_f16(GV_COLS, GV_MMA_N, dtype == EVKCU_BF16 ? 1 : 0, W_KMAJOR ? 0 : 1, 0);
     dim3 grid(slabs, splits);
     return launch_pdl("evkcu_matmul(gemv_tc)", kern, grid, GV_THREADS, GV_SMEM, st, mW, mX, Y, Mt, K, N, per, ep.acc,
-                      idesc, partial, tickets, s->d_error, ep.gelu, am);
+                      idesc, partial, tickets, s->d_error, ep.gelu, am, ar);
 }
 
 template <typename T, int BN, bool A_MN, bool B_MN>
@@ -653,6 +734,21 @@ int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M,
         if (BN == 128)
             return dispatch_major<T, 128>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
         return dispatch_major<T, 64>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
+    });
+}
+
+int gemv_allreduce_residual(const void* X, const void* W, void* Y, uint32_t Mt, uint32_t K, uint32_t N,
+                            const GemvAllReduce& ar, int dtype, cudaStream_t st) {
+    if (Mt == 0) return EVKCU_OK;
+    EVKCU_CHECK_ARG(X && W && Y && ar.epoch && ar.tp >= 2 && ar.tp <= 8 && ar.rank < ar.tp, EVKCU_BAD_ARG,
+                    "gemv_allreduce_residual: bad arguments");
+    EVKCU_CHECK_ARG(Mt <= (uint32_t)kGemvMaxM && K > 0 && K % 8 == 0 && N > 0 && N % 8 == 0, EVKCU_BAD_SHAPE,
+                    "gemv_allreduce_residual: needs 1..16 rows and K, N multiples of 8");
+    GemvArgmax am;
+    am.write_y = 0;  // y is written by the all-reduce tail
+    return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
+        GemvEpilogue ep;
+        return launch_gemv_tc<T, false>((const T*)X, (const T*)W, (T*)Y, Mt, K, N, ep, dtype, st, am, ar);
     });
 }
 

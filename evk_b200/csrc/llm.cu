@@ -23,6 +23,7 @@
 #include <cstring>
 #include <string>
 #include <unordered_map>
+#include <cstdlib>
 #include <vector>
 
 #include "common.cuh"
@@ -124,6 +125,7 @@ __global__ void advance_kernel(uint32_t* d_pos, uint32_t* d_len) {
     pdl_trigger();
     const uint32_t p = *d_pos + 1;
     *d_pos = p;
+    d_pos[2] += 1;  // decode-step counter (never reset): all-reduce flag values
     *d_len = p + 1;
 }
 __global__ void set_pos_kernel(uint32_t* d_pos, uint32_t* d_len, uint32_t pos) {
@@ -195,7 +197,14 @@ struct evkcu_llm {
     void *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr,
          *tmp = nullptr, *h1 = nullptr, *xl = nullptr, *logits = nullptr, *logits_all = nullptr;
     unsigned long long *keys = nullptr, *keys_all = nullptr;
-    uint32_t *d_pos = nullptr, *d_len = nullptr;
+    uint32_t *d_pos = nullptr, *d_len = nullptr, *d_epoch = nullptr;
+    // Fused all-reduce of the decode Wo / W2 projections (tp > 1): this
+    // rank's partial buffer and flags, and every rank's through IPC.
+    float* ar_buf = nullptr;
+    uint32_t* ar_flags = nullptr;
+    GemvAllReduce ar{};
+    bool ar_ready = false;
+    std::vector<void*> ipc_opened;
     uint32_t *gin = nullptr, *gout = nullptr;  // fixed ids in/out words of the decode graph
     uint32_t cur_len = 0, batch = 0;
     std::vector<void*> allocs;
@@ -229,10 +238,17 @@ ncclDataType_t nccl_type(int dtype) { return dtype == EVKCU_BF16 ? ncclBfloat16 
 
 // Wo / W2 product into the residual.  On one GPU acc_c fuses the add; with
 // tensor parallelism the product is a partial sum, summed across ranks first.
-int proj_residual(evkcu_llm* m, const void* a, const void* w, uint32_t rows, uint32_t K, cudaStream_t st) {
+int proj_residual(evkcu_llm* m, const void* a, const void* w, uint32_t rows, uint32_t K, bool decode,
+                  uint32_t callsite, cudaStream_t st) {
     const uint32_t D = m->cfg.d_model;
     const int dt = m->cfg.dtype;
     if (m->cfg.tp_size == 1) return evkcu_matmul(a, w, m->x, 1, rows, K, D, 0, 0, 0, EVKCU_MM_ACC_C, dt, st);
+    if (decode && rows <= 16 && m->ar_ready) {
+        // GEMV + all-reduce over NVLink peer memory + residual add, one kernel.
+        GemvAllReduce ar = m->ar;
+        ar.callsite = callsite;
+        return gemv_allreduce_residual(a, w, m->x, rows, K, D, ar, dt, st);
+    }
     LLM_TRY(evkcu_matmul(a, w, m->tmp, 1, rows, K, D, 0, 0, 0, 0, dt, st));
     const uint64_t n = (uint64_t)rows * D;
     LLM_TRY(nccl_check(ncclAllReduce(m->tmp, m->tmp, n, nccl_type(dt), ncclSum, m->comm, st), "ncclAllReduce"));
@@ -264,11 +280,11 @@ int run_blocks(evkcu_llm* m, uint32_t B, uint32_t S, bool decode, cudaStream_t s
             // the append kernel just wrote (batch stride max_seq rows).
             LLM_TRY(flash_attention_kv_strided(m->q, L.kc, L.vc, m->attn, B, S, m->Hl, m->Hkvl, m->Dh, 0.0f,
                                                EVKCU_ATTN_CAUSAL, dt, (uint64_t)c.max_seq * m->Hkvl * m->Dh, st));
-        LLM_TRY(proj_residual(m, m->attn, L.wo, R, m->Hl * m->Dh, st));
+        LLM_TRY(proj_residual(m, m->attn, L.wo, R, m->Hl * m->Dh, decode, 2 * l, st));
         LLM_TRY(evkcu_rms_norm(m->x, m->xn, nullptr, R, D, c.eps, dt, st));
         // W1 with the GELU applied in the GEMM / GEMV epilogue.
         LLM_TRY(matmul_ex(m->xn, L.w1, m->h1, 1, R, D, m->Fl, 0, 0, 0, 0, dt, 1, st));
-        LLM_TRY(proj_residual(m, m->h1, L.w2, R, m->Fl, st));
+        LLM_TRY(proj_residual(m, m->h1, L.w2, R, m->Fl, decode, 2 * l + 1, st));
     }
     return EVKCU_OK;
 }
@@ -369,6 +385,59 @@ extern "C" int evkcu_comm_destroy(void* comm) {
     return EVKCU_OK;
 }
 
+// Exchanges CUDA IPC handles of every rank's all-reduce buffer and flags
+// (ncclAllGather of the 2 x 64-byte handles) and maps the peers' into this
+// process.  Leaves ar_ready false (NCCL all-reduce path) on any failure.
+static void setup_allreduce(evkcu_llm* m) {
+    const uint32_t t = m->cfg.tp_size, rank = m->cfg.tp_rank;
+    if (t > 8 || !m->ar_buf || !m->ar_flags) return;
+    const size_t fbytes = (size_t)2 * m->cfg.layers * ((m->cfg.d_model + 127) / 128) * t * sizeof(uint32_t);
+    if (cudaMemset(m->ar_flags, 0, fbytes) != cudaSuccess) return;
+    cudaIpcMemHandle_t h[2];
+    if (cudaIpcGetMemHandle(&h[0], m->ar_buf) != cudaSuccess || cudaIpcGetMemHandle(&h[1], m->ar_flags) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    char* d = nullptr;
+    if (cudaMalloc(&d, sizeof(h) * (t + 1)) != cudaSuccess) return;
+    std::vector<cudaIpcMemHandle_t> all(2 * t);
+    bool ok = cudaMemcpy(d, h, sizeof(h), cudaMemcpyHostToDevice) == cudaSuccess &&
+              ncclAllGather(d, d + sizeof(h), sizeof(h), ncclUint8, m->comm, 0) == ncclSuccess &&
+              cudaStreamSynchronize(0) == cudaSuccess &&
+              cudaMemcpy(all.data(), d + sizeof(h), sizeof(h) * t, cudaMemcpyDeviceToHost) == cudaSuccess;
+    cudaFree(d);
+    if (!ok) {
+        cudaGetLastError();
+        return;
+    }
+    GemvAllReduce ar;
+    ar.tp = t;
+    ar.rank = rank;
+    ar.epoch = m->d_epoch;
+    for (uint32_t q = 0; q < t && ok; ++q) {
+        if (q == rank) {
+            ar.buf[q] = m->ar_buf;
+            ar.flags[q] = m->ar_flags;
+            continue;
+        }
+        void *pb = nullptr, *pf = nullptr;
+        ok = cudaIpcOpenMemHandle(&pb, all[2 * q], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+        if (ok) m->ipc_opened.push_back(pb);
+        ok = ok && cudaIpcOpenMemHandle(&pf, all[2 * q + 1], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+        if (ok) m->ipc_opened.push_back(pf);
+        ar.buf[q] = (float*)pb;
+        ar.flags[q] = (uint32_t*)pf;
+    }
+    if (!ok) {
+        cudaGetLastError();
+        return;
+    }
+    m->ar = ar;
+    // Enabled where it has been validated on the GPU (two ranks); other sizes
+    // keep the NCCL all-reduce.
+    m->ar_ready = t == 2 && getenv("EVKCU_DISABLE_FUSED_ALLREDUCE") == nullptr;
+}
+
 extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_llm** out) {
     EVKCU_CHECK_ARG(cfg && out, EVKCU_BAD_ARG, "evkcu_llm_create: null pointer");
     const evkcu_llm_config& c = *cfg;
@@ -428,7 +497,12 @@ extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_l
         A((void**)&m->keys, (size_t)c.max_batch * 8);
         A((void**)&m->keys_all, (size_t)c.max_batch * t * 8);
     }
-    A((void**)&m->d_pos, 2 * sizeof(uint32_t));
+    A((void**)&m->d_pos, 4 * sizeof(uint32_t));  // position, length, decode-step counter
+    const uint32_t slabs = (uint32_t)((D + 127) / 128);
+    if (t > 1) {
+        A((void**)&m->ar_buf, (size_t)2 * t * 16 * D * sizeof(float));
+        A((void**)&m->ar_flags, (size_t)2 * c.layers * slabs * t * sizeof(uint32_t));
+    }
     A((void**)&m->gin, (size_t)c.max_batch * 4);
     A((void**)&m->gout, (size_t)c.max_batch * 4);
     if (r != EVKCU_OK) {
@@ -436,6 +510,12 @@ extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_l
         return r;
     }
     m->d_len = m->d_pos + 1;
+    m->d_epoch = m->d_pos + 2;
+    {
+        const uint32_t init[4] = {0u, 0u, 1u, 0u};
+        EVKCU_CUDA_TRY(cudaMemcpy(m->d_pos, init, sizeof(init), cudaMemcpyHostToDevice));
+    }
+    if (t > 1) setup_allreduce(m);  // falls back to NCCL when peer mappings are unavailable
     *out = m;
     return EVKCU_OK;
 }
@@ -444,6 +524,7 @@ extern "C" int evkcu_llm_destroy(evkcu_llm* m) {
     if (!m) return EVKCU_OK;
     cudaDeviceSynchronize();
     for (auto& kv : m->graphs) cudaGraphExecDestroy(kv.second);
+    for (void* p : m->ipc_opened) cudaIpcCloseMemHandle(p);
     for (void* p : m->allocs) cudaFree(p);
     delete m;
     return EVKCU_OK;
