@@ -38,6 +38,16 @@ constexpr int kMaxStages = 8;
 constexpr uint32_t kDecSmemTarget = 96 * 1024;    // ring bytes: two CTAs per SM
 constexpr uint32_t kTimeoutDecode = 0x401;
 
+// 16-byte shared-memory load (one LDS.128; a warp reading 512 contiguous
+// bytes then takes the minimum 4 wavefronts).
+__device__ __forceinline__ Vec8 ld_shared_v4(const void* p) {
+    Vec8 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+                 : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+    return v;
+}
+
 __device__ __forceinline__ float ex2f(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -173,7 +183,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
                 for (int j = 0; j < SB; ++j) {
                     float kf[8];
                     if (dvalid) {
-                        unpack8<T>(*reinterpret_cast<const Vec8*>(kt + (r0 + (jb + j) * KPW) * Dh + d0), kf);
+                        unpack8<T>(ld_shared_v4(kt + (r0 + (jb + j) * KPW) * Dh + d0), kf);
                     } else {
 #pragma unroll
                         for (int e = 0; e < 8; ++e) kf[e] = 0.0f;
@@ -215,7 +225,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
                 for (int j = 0; j < SB; ++j) {
                     float vf[8];
                     if (dvalid) {
-                        unpack8<T>(*reinterpret_cast<const Vec8*>(vt + (r0 + (jb + j) * KPW) * Dh + d0), vf);
+                        unpack8<T>(ld_shared_v4(vt + (r0 + (jb + j) * KPW) * Dh + d0), vf);
                     } else {
 #pragma unroll
                         for (int e = 0; e < 8; ++e) vf[e] = 0.0f;

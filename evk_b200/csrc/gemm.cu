@@ -579,11 +579,15 @@ int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32
     // of loads in flight), leaving the SM's other slot to the next kernel of
     // a decode chain, which (programmatic dependent launch) streams its own
     // weights meanwhile.  Larger weights: two CTAs per SM.  Whole k-tiles per
-    // split, at least 4 where K allows (each split adds a partial to the
-    // combine).
-    const uint32_t per_sm = (uint64_t)K * N * sizeof(T) < (64ull << 20) ? 1u : 2u;
+    // split, at least 4 for weights of 16 MB and more (each split adds a
+    // partial to the combine).
+    const uint64_t wbytes = (uint64_t)K * N * sizeof(T);
+    const uint32_t per_sm = wbytes < (64ull << 20) ? 1u : 2u;
     const uint32_t slots = per_sm * (uint32_t)s->sm_count;
-    uint32_t splits = std::max<uint32_t>(1, std::min<uint32_t>(std::max<uint32_t>(1, ktiles / 4), slots / slabs));
+    // Tiny weights (< 16 MB) are pure latency: as many CTAs as there are slots.
+    const uint32_t min_tiles = wbytes < (16ull << 20) ? 1u : 4u;
+    uint32_t splits =
+        std::max<uint32_t>(1, std::min<uint32_t>(std::max<uint32_t>(1, ktiles / min_tiles), slots / slabs));
     const uint32_t per = (ktiles + splits - 1) / splits;
     splits = (ktiles + per - 1) / per;
     CUtensorMap mW, mX;
