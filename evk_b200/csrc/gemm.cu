@@ -69,8 +69,22 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const uint32_t n0 = blockIdx.x * BN;
-    const uint32_t m0 = blockIdx.y * BM;
+    // Raster: groups of kGroupM row tiles, row tile fastest within a group,
+    // so the CTAs in flight share a few B column tiles and a group's A rows
+    // stay in L2 while B streams past once per group (B is read
+    // ceil(row tiles / kGroupM) times instead of once per wave of rows).
+    constexpr uint32_t kGroupM = 16;
+    uint32_t n0, m0;
+    {
+        const uint32_t nt = gridDim.x, mt = gridDim.y;
+        const uint32_t lin = blockIdx.y * nt + blockIdx.x;
+        const uint32_t per_group = kGroupM * nt;
+        const uint32_t grp = lin / per_group, first_m = grp * kGroupM;
+        const uint32_t gm = min(kGroupM, mt - first_m);  // rows in this (possibly last) group
+        const uint32_t in = lin % per_group;
+        m0 = (first_m + in % gm) * BM;
+        n0 = (in / gm) * BN;
+    }
     const uint32_t bz = blockIdx.z;
     const int za = bcastA ? 0 : (int)bz;
     const int zb = bcastB ? 0 : (int)bz;
@@ -146,7 +160,11 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
     } else {
         // Epilogue warps 2..5 own TMEM lane quarters (warp % 4).
         const int q = warp & 3;
-        const bool ok = mbar_wait(accum, 0, s_abort, err, kTimeoutGemm);
+        // Lane 0 waits (128 pollers on one barrier word would keep the shared
+        // memory banks busy during the whole mainloop); the warp follows.
+        const bool ok = __shfl_sync(0xffffffffu,
+                                    lane == 0 ? (int)mbar_wait_sleep(accum, 0, s_abort, err, kTimeoutGemm) : 0,
+                                    0) != 0;
         tc_fence_after();
         if (ok) {
             const uint32_t row = m0 + q * 32 + lane;

@@ -71,6 +71,42 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait that may suspend the thread for up to `ns` nanoseconds while the
+// phase is incomplete (it resumes as soon as the phase completes).
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for a long-lived phase (e.g. a whole GEMM mainloop): the
+// waiting thread sleeps in try_wait between checks instead of polling the
+// barrier word.  Same failure behaviour as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                unsigned int* err, unsigned int code) {
+    const uint32_t a = smem_u32(bar);
+    const long long t0 = clock64();
+    while (!mbar_try_wait_hint(a, parity, 20000u)) {
+        if (*abort) return false;
+        if (err && *reinterpret_cast<volatile unsigned int*>(err)) {
+            *abort = 1;
+            return false;
+        }
+        if (clock64() - t0 > kSpinLimitCycles) {
+            *abort = 1;
+            if (err) atomicCAS(err, 0u, code);
+            return false;
+        }
+    }
+    return true;
+}
+
 // Bounded wait for the phase with the given parity.  Returns false (and
 // records `code` in the device error word and in *abort) if the phase did
 // not complete within kSpinLimitCycles or another role already aborted.
