@@ -213,11 +213,28 @@ struct GemvAllReduce {
 int gemv_allreduce_residual(const void* X, const void* W, void* Y, uint32_t Mt, uint32_t K, uint32_t N,
                             const GemvAllReduce& ar, int dtype, cudaStream_t st);
 
+// Epilogue of the fused QKV projection of the LLM driver: the output row r
+// (sequence r / S, position pos + r % S with pos = *d_pos when given, else
+// pos0) has columns [q heads | k heads | v heads] of Dh each; q and k are
+// rotated per head (adjacent pairs (2p, 2p + 1), angle position *
+// base^(-2p / Dh), as evk::ai::rope with head_dim = Dh), q goes to
+// q[r, Hq * Dh], k and v to row b * max_len + position of the caches
+// [B, max_len, Hk * Dh].  The product itself is not stored.
+struct QkvRope {
+    void* q = nullptr;
+    void* kc = nullptr;
+    void* vc = nullptr;
+    uint32_t Hq = 0, Hk = 0, Dh = 0, S = 1, max_len = 0, pos0 = 0;
+    const uint32_t* d_pos = nullptr;
+    float base = 10000.0f;
+};
+
 // evkcu_matmul with an optional GELU applied to each output element (after
-// the optional C +=), for the library's own drivers.
+// the optional C +=), or the QKV epilogue above, for the library's own
+// drivers.
 int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M, uint32_t K, uint32_t N,
               uint64_t stride_a, uint64_t stride_b, uint64_t stride_c, uint32_t flags, int dtype, int gelu,
-              void* stream);
+              void* stream, const QkvRope* qkv = nullptr);
 
 // evkcu_flash_attention with K and V read at a batch stride of kv_bstride
 // elements (0: N * Hkv * Dh, contiguous), e.g. the first N rows of each

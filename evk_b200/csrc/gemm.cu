@@ -38,6 +38,38 @@ constexpr int BK = 64;
 constexpr int kGemmThreads = 192;
 constexpr uint32_t kTimeoutGemm = 0x101;
 
+// ------------------------------------------------- fused QKV epilogue ----
+// Inverse frequencies base^(-2p / Dh) for p < Dh / 2, once per CTA.
+__device__ __forceinline__ void qkv_fill_inv_freq(const QkvRope& qr, float* inv_freq) {
+    if (!qr.q) return;
+    for (uint32_t p = threadIdx.x; p < qr.Dh / 2; p += blockDim.x)
+        inv_freq[p] = powf(qr.base, -2.0f * (float)p / (float)qr.Dh);
+}
+
+// Destination of output (row, col) of the fused QKV projection (see QkvRope);
+// nullptr when the cache row lies beyond max_len.
+template <typename T>
+__device__ __forceinline__ T* qkv_dst(const QkvRope& qr, uint32_t pos_base, uint32_t row, uint32_t col) {
+    const uint32_t qcols = qr.Hq * qr.Dh, kcols = qr.Hk * qr.Dh;
+    if (col < qcols) return reinterpret_cast<T*>(qr.q) + (uint64_t)row * qcols + col;
+    const uint32_t b = row / qr.S, pos = pos_base + row % qr.S;
+    if (pos >= qr.max_len) return nullptr;
+    const bool is_k = col < qcols + kcols;
+    const uint32_t c = is_k ? col - qcols : col - qcols - kcols;
+    return reinterpret_cast<T*>(is_k ? qr.kc : qr.vc) + ((uint64_t)b * qr.max_len + pos) * kcols + c;
+}
+
+// Rotates the pair (x0, x1) = columns (2p, 2p + 1) of a q / k head.
+__device__ __forceinline__ void qkv_rotate(const QkvRope& qr, const float* inv_freq, uint32_t pos_base, uint32_t row,
+                                           uint32_t col, float& x0, float& x1) {
+    const float t = (float)(pos_base + row % qr.S);
+    float sn, cs;
+    sincosf(t * inv_freq[(col % qr.Dh) >> 1], &sn, &cs);
+    const float a = x0 * cs - x1 * sn, b = x0 * sn + x1 * cs;
+    x0 = a;
+    x1 = b;
+}
+
 // CPS = CTAs per SM: 1 (a ~196 KB ring) or 2 (~96 KB each: one CTA's
 // epilogue runs while the other's MMAs keep the tensor core busy).
 template <int BN, int CPS>
@@ -54,8 +86,9 @@ template <typename T, int BN, bool A_MN, bool B_MN, int CPS>
 __global__ void __launch_bounds__(kGemmThreads, CPS)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, T* __restrict__ C,
                    uint32_t M, uint32_t N, uint32_t K, uint64_t strideC, int bcastA, int bcastB, int acc_c,
-                   uint32_t idesc, unsigned int* err, int gelu) {
+                   uint32_t idesc, unsigned int* err, int gelu, QkvRope qr) {
     using Cfg = GemmCfg<BN, CPS>;
+    __shared__ float s_inv_freq[128];
     constexpr int STAGES = Cfg::STAGES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -105,6 +138,7 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
         tmem_alloc(s_tmem, BN);
         tmem_relinquish();
     }
+    qkv_fill_inv_freq(qr, s_inv_freq);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -166,6 +200,7 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
                                     lane == 0 ? (int)mbar_wait_sleep(accum, 0, s_abort, err, kTimeoutGemm) : 0,
                                     0) != 0;
         tc_fence_after();
+        const uint32_t pos_base = qr.q ? (qr.d_pos ? *qr.d_pos : qr.pos0) : 0u;
         if (ok) {
             const uint32_t row = m0 + q * 32 + lane;
             T* crow = C + (uint64_t)bz * strideC + (uint64_t)row * N;
@@ -182,6 +217,16 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
                             float f[8];
 #pragma unroll
                             for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[g * 8 + e]);
+                            if (qr.q) {
+                                if (col < (qr.Hq + qr.Hk) * qr.Dh) {
+#pragma unroll
+                                    for (int e = 0; e < 8; e += 2)
+                                        qkv_rotate(qr, s_inv_freq, pos_base, row, col + e, f[e], f[e + 1]);
+                                }
+                                T* qd = qkv_dst<T>(qr, pos_base, row, col);
+                                if (qd) *reinterpret_cast<Vec8*>(qd) = pack8<T>(f);
+                                continue;
+                            }
                             Vec8* dst = reinterpret_cast<Vec8*>(crow + col);
                             if (acc_c) {
                                 float o[8];
@@ -240,7 +285,8 @@ template <typename T>
 __device__ void gemv_argmax_tail(const float* s_val, uint32_t Mt, uint32_t N, uint32_t n0, const GemvArgmax& am);
 template <typename T>
 __device__ void gemv_combine_splits(const float* __restrict__ partial, T* __restrict__ Y, uint32_t Mt, uint32_t N,
-                                    uint32_t n0, int acc_c, int gelu, int write_y, float* s_val, bool raw);
+                                    uint32_t n0, int acc_c, int gelu, int write_y, float* s_val, bool raw,
+                                    const QkvRope& qr, const float* inv_freq);
 template <typename T>
 __device__ void gemv_allreduce_tail(const float* s_val, T* __restrict__ Y, uint32_t Mt, uint32_t N, uint32_t n0,
                                     const GemvAllReduce& ar, unsigned int* err);
@@ -250,7 +296,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
     gemv_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
                    T* __restrict__ Y, uint32_t Mt, uint32_t K, uint32_t N, uint32_t ktiles_per_cta, int acc_c,
                    uint32_t idesc, float* __restrict__ partial, unsigned int* __restrict__ tickets,
-                   unsigned int* err, int gelu, GemvArgmax am, GemvAllReduce ar) {
+                   unsigned int* err, int gelu, GemvArgmax am, GemvAllReduce ar, QkvRope qr) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sW = smem;
@@ -261,6 +307,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
     uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accum + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
     __shared__ bool is_last;
+    __shared__ float s_inv_freq[128];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t n0 = blockIdx.x * GV_COLS;
@@ -284,6 +331,7 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
         tmem_alloc(s_tmem, 32);
         tmem_relinquish();
     }
+    qkv_fill_inv_freq(qr, s_inv_freq);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -368,7 +416,23 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
             for (int m = 0; m < GV_MMA_N; ++m) v[m] = __uint_as_float(r[m]);
         }
         tc_fence_before();
-        if (have && gridDim.y == 1) {
+        if (have && gridDim.y == 1 && qr.q) {
+            // Fused QKV: rotate with the partner column (adjacent lane),
+            // store to q or the caches.
+            const uint32_t n = n0 + nn;
+            const uint32_t pos_base = qr.d_pos ? *qr.d_pos : qr.pos0;
+            const bool rot = n < (qr.Hq + qr.Hk) * qr.Dh;
+#pragma unroll
+            for (int m = 0; m < GV_MMA_N; ++m) {
+                const float partner = __shfl_xor_sync(0xffffffffu, v[m], 1);
+                if (m < (int)Mt && n < N) {
+                    float x0 = (n & 1) ? partner : v[m], x1 = (n & 1) ? v[m] : partner;
+                    if (rot) qkv_rotate(qr, s_inv_freq, pos_base, m, n & ~1u, x0, x1);
+                    T* qd = qkv_dst<T>(qr, pos_base, m, n);
+                    if (qd) *qd = Elem<T>::from_f((n & 1) ? x1 : x0);
+                }
+            }
+        } else if (have && gridDim.y == 1) {
             const uint32_t n = n0 + nn;
             // With an argmax the TMA ring (idle now) stages the stored values.
             float* s_val = reinterpret_cast<float*>(smem);  // [GV_MMA_N][GV_COLS]
@@ -407,7 +471,8 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
         if (!is_last) return;
         __threadfence();
         gemv_combine_splits<T>(partial, Y, Mt, N, n0, acc_c, gelu, am.write_y,
-                               (am.slab_keys || ar.tp) ? reinterpret_cast<float*>(smem) : nullptr, ar.tp != 0);
+                               (am.slab_keys || ar.tp) ? reinterpret_cast<float*>(smem) : nullptr, ar.tp != 0, qr,
+                               s_inv_freq);
         if (threadIdx.x == 0) tickets[blockIdx.x] = 0u;
     }
     if (am.slab_keys) gemv_argmax_tail<T>(reinterpret_cast<const float*>(smem), Mt, N, n0, am);
@@ -543,7 +608,8 @@ __device__ void gemv_argmax_tail(const float* s_val, uint32_t Mt, uint32_t N, ui
 // the epilogue; optionally stages the stored values for the argmax.
 template <typename T>
 __device__ void gemv_combine_splits(const float* __restrict__ partial, T* __restrict__ Y, uint32_t Mt, uint32_t N,
-                                    uint32_t n0, int acc_c, int gelu, int write_y, float* s_val, bool raw) {
+                                    uint32_t n0, int acc_c, int gelu, int write_y, float* s_val, bool raw,
+                                    const QkvRope& qr, const float* inv_freq) {
     // Thread g takes 4 consecutive outputs (one float4 of every split's
     // partial) and keeps up to 16 splits' loads in flight before adding them
     // in split order, so the combine costs a few L2 round trips, not one per
@@ -568,7 +634,22 @@ __device__ void gemv_combine_splits(const float* __restrict__ partial, T* __rest
                 }
             }
         }
-        const float sums[4] = {acc.x, acc.y, acc.z, acc.w};
+        float sums[4] = {acc.x, acc.y, acc.z, acc.w};
+        if (qr.q) {
+            // Fused QKV: columns 4g .. 4g + 3 hold two rotation pairs.
+            const uint32_t m = (g * 4) / GV_COLS, n = n0 + (g * 4) % GV_COLS;
+            if (n >= N) continue;
+            const uint32_t pos_base = qr.d_pos ? *qr.d_pos : qr.pos0;
+            if (n < (qr.Hq + qr.Hk) * qr.Dh) {
+                qkv_rotate(qr, inv_freq, pos_base, m, n, sums[0], sums[1]);
+                qkv_rotate(qr, inv_freq, pos_base, m, n + 2, sums[2], sums[3]);
+            }
+            T* qd = qkv_dst<T>(qr, pos_base, m, n);
+            if (qd)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) qd[e] = Elem<T>::from_f(sums[e]);
+            continue;
+        }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const uint32_t i = g * 4 + e;
@@ -592,7 +673,8 @@ __device__ void gemv_combine_splits(const float* __restrict__ partial, T* __rest
 
 template <typename T, bool W_KMAJOR>
 int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, GemvEpilogue ep, int dtype,
-                   cudaStream_t st, GemvArgmax am = GemvArgmax(), const GemvAllReduce& ar = GemvAllReduce()) {
+                   cudaStream_t st, GemvArgmax am = GemvArgmax(), const GemvAllReduce& ar = GemvAllReduce(),
+                   const QkvRope& qr = QkvRope()) {
     DeviceState* s = state();
     const uint32_t slabs = (N + GV_COLS - 1) / GV_COLS;
     const uint32_t ktiles = (K + GV_BK - 1) / GV_BK;
@@ -644,12 +726,13 @@ int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32
     const uint32_t idesc = make_idesc_f16(GV_COLS, GV_MMA_N, dtype == EVKCU_BF16 ? 1 : 0, W_KMAJOR ? 0 : 1, 0);
     dim3 grid(slabs, splits);
     return launch_pdl("evkcu_matmul(gemv_tc)", kern, grid, GV_THREADS, GV_SMEM, st, mW, mX, Y, Mt, K, N, per, ep.acc,
-                      idesc, partial, tickets, s->d_error, ep.gelu, am, ar);
+                      idesc, partial, tickets, s->d_error, ep.gelu, am, ar, qr);
 }
 
 template <typename T, int BN, bool A_MN, bool B_MN, int CPS>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch, uint32_t M, uint32_t N, uint32_t K,
-              uint64_t strideC, int bcastA, int bcastB, int acc, int is_bf16, int gelu, cudaStream_t st) {
+              uint64_t strideC, int bcastA, int bcastB, int acc, int is_bf16, int gelu, const QkvRope& qr,
+              cudaStream_t st) {
     using Cfg = GemmCfg<BN, CPS>;
     static bool attr_set = false;
     auto kern = gemm_tc_kernel<T, BN, A_MN, B_MN, CPS>;
@@ -660,39 +743,44 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
     uint32_t idesc = make_idesc_f16(BM, BN, is_bf16, A_MN, B_MN);
     kern<<<grid, kGemmThreads, Cfg::SMEM, st>>>(ta, tb, C, M, N, K, strideC, bcastA, bcastB, acc, idesc,
-                                                state()->d_error, gelu);
+                                                state()->d_error, gelu, qr);
     return after_launch("evkcu_matmul(tcgen05)");
 }
 
 template <typename T, int BN, int CPS>
 int dispatch_major_c(bool ta, bool tb, const CUtensorMap& mA, const CUtensorMap& mB, T* C, uint32_t batch, uint32_t M,
-                     uint32_t N, uint32_t K, uint64_t sC, int bA, int bB, int acc, int bf, int gelu, cudaStream_t st) {
-    if (!ta && !tb) return launch_tc<T, BN, false, true, CPS>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
-    if (!ta && tb) return launch_tc<T, BN, false, false, CPS>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
-    if (ta && !tb) return launch_tc<T, BN, true, true, CPS>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
-    return launch_tc<T, BN, true, false, CPS>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
+                     uint32_t N, uint32_t K, uint64_t sC, int bA, int bB, int acc, int bf, int gelu, const QkvRope& qr,
+                     cudaStream_t st) {
+    if (!ta && !tb)
+        return launch_tc<T, BN, false, true, CPS>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, qr, st);
+    if (!ta && tb)
+        return launch_tc<T, BN, false, false, CPS>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, qr, st);
+    if (ta && !tb)
+        return launch_tc<T, BN, true, true, CPS>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, qr, st);
+    return launch_tc<T, BN, true, false, CPS>(mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, qr, st);
 }
 
 template <typename T, int BN>
 int dispatch_major(bool ta, bool tb, const CUtensorMap& mA, const CUtensorMap& mB, T* C, uint32_t batch, uint32_t M,
-                   uint32_t N, uint32_t K, uint64_t sC, int bA, int bB, int acc, int bf, int gelu, cudaStream_t st) {
+                   uint32_t N, uint32_t K, uint64_t sC, int bA, int bB, int acc, int bf, int gelu, const QkvRope& qr,
+                   cudaStream_t st) {
     // Long K with narrow N (the MLP down-projections): one CTA per SM, whose
     // deeper ring wins (measured 1.42 vs 1.25 PFLOP/s at 16384x8192x2048);
     // otherwise two, overlapping epilogues (1.32 vs 1.29 at 8192^3).
     if (K >= 8192 && N <= 4096)
-        return dispatch_major_c<T, BN, 1>(ta, tb, mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
-    return dispatch_major_c<T, BN, 2>(ta, tb, mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
+        return dispatch_major_c<T, BN, 1>(ta, tb, mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, qr, st);
+    return dispatch_major_c<T, BN, 2>(ta, tb, mA, mB, C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, qr, st);
 }
 
 template <typename T>
 int launch_gemv(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t N, bool tb, int acc, int gelu,
-                cudaStream_t st) {
+                const QkvRope& qr, cudaStream_t st) {
     const int dtype = std::is_same<T, __nv_bfloat16>::value ? EVKCU_BF16 : EVKCU_F16;
     GemvEpilogue ep;
     ep.acc = acc;
     ep.gelu = gelu;
-    if (tb) return launch_gemv_tc<T, true>(X, W, Y, Mt, K, N, ep, dtype, st);
-    return launch_gemv_tc<T, false>(X, W, Y, Mt, K, N, ep, dtype, st);
+    if (tb) return launch_gemv_tc<T, true>(X, W, Y, Mt, K, N, ep, dtype, st, GemvArgmax(), GemvAllReduce(), qr);
+    return launch_gemv_tc<T, false>(X, W, Y, Mt, K, N, ep, dtype, st, GemvArgmax(), GemvAllReduce(), qr);
 }
 
 }  // namespace
@@ -705,7 +793,13 @@ namespace evkcu {
 
 int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M, uint32_t K, uint32_t N,
               uint64_t stride_a, uint64_t stride_b, uint64_t stride_c, uint32_t flags, int dtype, int gelu,
-              void* stream) {
+              void* stream, const QkvRope* qkv) {
+    const QkvRope qr = qkv ? *qkv : QkvRope();
+    if (qkv) {
+        EVKCU_CHECK_ARG(qkv->q && qkv->kc && qkv->vc && qkv->Dh % 8 == 0 && qkv->Dh / 2 <= 128 && qkv->S > 0 &&
+                            N == (qkv->Hq + 2 * qkv->Hk) * qkv->Dh && batch == 1 && !(flags & EVKCU_MM_ACC_C),
+                        EVKCU_BAD_ARG, "matmul_ex: bad fused QKV arguments");
+    }
     if (batch == 0 || M == 0 || N == 0) return EVKCU_OK;
     EVKCU_CHECK_ARG(A && B && C, EVKCU_BAD_ARG, "evkcu_matmul: null pointer");
     EVKCU_CHECK_ARG(dtype == EVKCU_F16 || dtype == EVKCU_BF16, EVKCU_BAD_ARG, "evkcu_matmul: unknown dtype");
@@ -734,7 +828,7 @@ int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M,
     const uint64_t Mt = (uint64_t)batch * M;
     if (!ta && Mt <= kGemvMaxM && (batch == 1 || stride_b == 0) && a_contig && c_contig) {
         return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-            return launch_gemv<T>((const T*)A, (const T*)B, (T*)C, (uint32_t)Mt, K, N, tb, acc, gelu, st);
+            return launch_gemv<T>((const T*)A, (const T*)B, (T*)C, (uint32_t)Mt, K, N, tb, acc, gelu, qr, st);
         });
     }
 
@@ -766,10 +860,10 @@ int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M,
     const uint64_t sC = batch > 1 ? stride_c : 0;
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
         if (BN == 256)
-            return dispatch_major<T, 256>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
+            return dispatch_major<T, 256>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, qr, st);
         if (BN == 128)
-            return dispatch_major<T, 128>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
-        return dispatch_major<T, 64>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, st);
+            return dispatch_major<T, 128>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, qr, st);
+        return dispatch_major<T, 64>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, qr, st);
     });
 }
 

@@ -66,59 +66,6 @@ __global__ void fill_normal_kernel(T* dst, uint32_t rows, uint32_t cols, uint64_
     }
 }
 
-// One thread per 8 consecutive elements of a row of qkv [R, (Hq + 2 Hk) * Dh]
-// (q heads, k heads, v heads).  Row r belongs to sequence r / S at position
-// pos0 + r % S (pos0 from *d_pos when given).  q and k are rotated per head
-// (pair p: angle pos * base^(-2p/Dh), as evk::ai::rope with head_dim = Dh;
-// the Dh/2 inverse frequencies are computed once per block); q goes to
-// q_out [R, Hq Dh]; k and v go to the cache [B, max_len, Hk Dh] at their
-// position.
-template <typename T>
-__global__ void qkv_rope_append_kernel(const T* __restrict__ qkv, uint32_t R, uint32_t S, uint32_t pos0,
-                                       const uint32_t* __restrict__ d_pos, uint32_t Hq, uint32_t Hk, uint32_t Dh,
-                                       float base, T* __restrict__ q_out, T* __restrict__ kcache,
-                                       T* __restrict__ vcache, uint32_t max_len) {
-    __shared__ float s_inv_freq[128];  // Dh <= 256
-    for (uint32_t p = threadIdx.x; p < Dh / 2; p += blockDim.x)
-        s_inv_freq[p] = powf(base, -2.0f * (float)p / (float)Dh);
-    __syncthreads();
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
-    const uint32_t C = (Hq + 2 * Hk) * Dh;
-    const uint32_t per_row = C / 8;
-    const uint32_t p0 = d_pos ? *d_pos : pos0;
-    const uint64_t total = (uint64_t)R * per_row;
-    for (uint64_t w = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; w < total; w += (uint64_t)gridDim.x * blockDim.x) {
-        const uint32_t r = (uint32_t)(w / per_row);
-        const uint32_t c0 = (uint32_t)(w % per_row) * 8;
-        const uint32_t b = r / S;
-        const uint32_t pos = p0 + r % S;
-        float f[8];
-        unpack8<T>(*reinterpret_cast<const Vec8*>(qkv + (uint64_t)r * C + c0), f);
-        const bool is_v = c0 >= (Hq + Hk) * Dh;
-        if (!is_v) {
-            const float t = (float)pos;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const uint32_t p = ((c0 % Dh) >> 1) + k;
-                float sn, cs;
-                sincosf(t * s_inv_freq[p], &sn, &cs);
-                const float x0 = f[2 * k], x1 = f[2 * k + 1];
-                f[2 * k] = x0 * cs - x1 * sn;
-                f[2 * k + 1] = x0 * sn + x1 * cs;
-            }
-        }
-        const Vec8 v8 = pack8<T>(f);
-        if (c0 < Hq * Dh) {
-            *reinterpret_cast<Vec8*>(q_out + (uint64_t)r * Hq * Dh + c0) = v8;
-        } else {
-            const uint32_t kc = is_v ? c0 - (Hq + Hk) * Dh : c0 - Hq * Dh;
-            const uint64_t crow = ((uint64_t)b * max_len + pos) * Hk * Dh + kc;
-            if (pos < max_len) *reinterpret_cast<Vec8*>((is_v ? vcache : kcache) + crow) = v8;
-        }
-    }
-}
-
 // After a decode step: one more cached position.
 __global__ void advance_kernel(uint32_t* d_pos, uint32_t* d_len) {
     pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
@@ -194,7 +141,7 @@ struct evkcu_llm {
     void* emb = nullptr;
     void* lm_head = nullptr;  // [D, Vl] when untied
     std::vector<LlmLayer> layers;
-    void *x = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr,
+    void *x = nullptr, *xn = nullptr, *q = nullptr, *attn = nullptr,
          *tmp = nullptr, *h1 = nullptr, *xl = nullptr, *logits = nullptr, *logits_all = nullptr;
     unsigned long long *keys = nullptr, *keys_all = nullptr;
     uint32_t *d_pos = nullptr, *d_len = nullptr, *d_epoch = nullptr;
@@ -265,13 +212,21 @@ int run_blocks(evkcu_llm* m, uint32_t B, uint32_t S, bool decode, cudaStream_t s
     for (uint32_t l = 0; l < c.layers; ++l) {
         LlmLayer& L = m->layers[l];
         LLM_TRY(evkcu_rms_norm(m->x, m->xn, nullptr, R, D, c.eps, dt, st));
-        LLM_TRY(evkcu_matmul(m->xn, L.wqkv, m->qkv, 1, R, D, m->C, 0, 0, 0, 0, dt, st));
-        const uint64_t items = (uint64_t)R * (m->C / 8);
-        LLM_TRY(EVKCU_DISPATCH_DTYPE(dt, T, [&] {
-            return launch_pdl("llm qkv_rope_append", qkv_rope_append_kernel<T>, grid_for_items(items), kT, 0, st,
-                              (const T*)m->qkv, R, S, 0u, decode ? (const uint32_t*)m->d_pos : nullptr, m->Hl,
-                              m->Hkvl, m->Dh, c.rope_base, (T*)m->q, (T*)L.kc, (T*)L.vc, c.max_seq);
-        }));
+        // QKV projection whose epilogue applies RoPE to q and k and writes q
+        // and the cache rows directly (the [R, C] product is never stored).
+        QkvRope qr;
+        qr.q = m->q;
+        qr.kc = L.kc;
+        qr.vc = L.vc;
+        qr.Hq = m->Hl;
+        qr.Hk = m->Hkvl;
+        qr.Dh = m->Dh;
+        qr.S = S;
+        qr.max_len = c.max_seq;
+        qr.pos0 = 0;
+        qr.d_pos = decode ? m->d_pos : nullptr;
+        qr.base = c.rope_base;
+        LLM_TRY(matmul_ex(m->xn, L.wqkv, m->q /* not written */, 1, R, D, m->C, 0, 0, 0, 0, dt, 0, st, &qr));
         if (decode)
             LLM_TRY(evkcu_single_query_attention_devlen(m->q, L.kc, L.vc, m->attn, B, m->Hl, m->Hkvl, m->Dh,
                                                          c.max_seq, m->d_len, 0.0f, dt, st));
@@ -485,7 +440,6 @@ extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_l
     }
     A(&m->x, R * D * kE);
     A(&m->xn, R * D * kE);
-    A(&m->qkv, R * m->C * kE);
     A(&m->q, R * m->Hl * Dh * kE);
     A(&m->attn, R * m->Hl * Dh * kE);
     if (t > 1) A(&m->tmp, R * D * kE);
