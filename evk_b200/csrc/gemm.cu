@@ -616,6 +616,35 @@ __device__ void gemv_combine_splits(const float* __restrict__ partial, T* __rest
     // split.
     const float* base = partial + (uint64_t)blockIdx.x * gridDim.y * (GV_MMA_N * GV_COLS);
     const uint32_t groups = Mt * GV_COLS / 4;
+    if (groups < blockDim.x && !qr.q) {
+        // Few rows: one output per thread keeps more threads loading.
+        for (uint32_t i = threadIdx.x; i < Mt * GV_COLS; i += blockDim.x) {
+            const uint32_t m = i / GV_COLS, c = i % GV_COLS, n = n0 + c;
+            float sum = 0.0f;
+            for (uint32_t y0 = 0; y0 < gridDim.y; y0 += 8) {
+                float t[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    t[j] = y0 + j < gridDim.y ? __ldcg(base + (uint64_t)(y0 + j) * (GV_MMA_N * GV_COLS) + i) : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (y0 + j < gridDim.y) sum += t[j];
+            }
+            if (raw) {
+                s_val[m * GV_COLS + c] = sum;
+                continue;
+            }
+            if (n < N) {
+                if (acc_c) sum += Elem<T>::to_f(Y[(uint64_t)m * N + n]);
+                if (gelu) sum = gelu_f(sum);
+                const T st = Elem<T>::from_f(sum);
+                if (write_y) Y[(uint64_t)m * N + n] = st;
+                sum = Elem<T>::to_f(st);
+            }
+            if (s_val) s_val[m * GV_COLS + c] = sum;
+        }
+        return;
+    }
     for (uint32_t g = threadIdx.x; g < groups; g += blockDim.x) {
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         for (uint32_t y0 = 0; y0 < gridDim.y; y0 += 16) {
