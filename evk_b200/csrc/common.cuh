@@ -64,6 +64,7 @@ struct DeviceState {
     void* ws[WS_COUNT] = {};
     size_t ws_bytes[WS_COUNT] = {};
     bool pdl = true;  // programmatic dependent launch for the decode-path kernels
+    bool plain_epilogue = false;  // GEMM: per-row stores instead of the staged TMA epilogue
 };
 // Returns the state of the current device, creating it on first use.
 DeviceState* state();
@@ -134,6 +135,21 @@ template <> struct Elem<__nv_bfloat16> {
 struct __align__(16) Vec8 {
     uint32_t w[4];
 };
+
+// 16-byte shared-memory accesses (one LDS.128 / STS.128 each).
+__device__ __forceinline__ Vec8 ld_shared_vec8(const void* p) {
+    Vec8 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3])
+                 : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p)))
+                 : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_shared_vec8(void* p, const Vec8& v) {
+    asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))),
+                 "r"(v.w[0]), "r"(v.w[1]), "r"(v.w[2]), "r"(v.w[3])
+                 : "memory");
+}
 
 template <typename T>
 __device__ __forceinline__ void unpack8(const Vec8& v, float (&f)[8]) {
@@ -219,7 +235,10 @@ int gemv_allreduce_residual(const void* X, const void* W, void* Y, uint32_t Mt, 
 // rotated per head (adjacent pairs (2p, 2p + 1), angle position *
 // base^(-2p / Dh), as evk::ai::rope with head_dim = Dh), q goes to
 // q[r, Hq * Dh], k and v to row b * max_len + position of the caches
-// [B, max_len, Hk * Dh].  The product itself is not stored.
+// [B, max_len, Hk * Dh].  The product itself is not stored.  With `cs`, the
+// (cos, sin) of each angle come from a table [cs_len][Dh / 2] filled by
+// rope_table() (the same fp32 expressions, so the same values) instead of
+// a sincosf per pair.
 struct QkvRope {
     void* q = nullptr;
     void* kc = nullptr;
@@ -227,7 +246,13 @@ struct QkvRope {
     uint32_t Hq = 0, Hk = 0, Dh = 0, S = 1, max_len = 0, pos0 = 0;
     const uint32_t* d_pos = nullptr;
     float base = 10000.0f;
+    const float2* cs = nullptr;
+    uint32_t cs_len = 0;
 };
+
+// Fills cs[pos][p] = (cos, sin)(pos * base^(-2p / Dh)) for pos < len,
+// p < Dh / 2, in the fused QKV epilogue's own arithmetic.
+int rope_table(float2* cs, uint32_t len, uint32_t Dh, float base, cudaStream_t st);
 
 // evkcu_matmul with an optional GELU applied to each output element (after
 // the optional C +=), or the QKV epilogue above, for the library's own

@@ -69,8 +69,8 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
     T* __restrict__ out, uint32_t H, uint32_t Hkv, uint32_t Dh, uint32_t max_len, uint32_t cur_len,
     const uint32_t* __restrict__ d_cur_len, uint32_t chunk, float scale_log2, uint32_t stages,
     float* __restrict__ partial, unsigned int* __restrict__ tickets, unsigned int* err) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     constexpr int KPW = DecTile<LPK>::KPW, ROWS = DecTile<LPK>::ROWS, STEPS = DecTile<LPK>::STEPS;
     constexpr int NW = kDecCompute;
     __shared__ float sm_m[NW][G], sm_l[NW][G];

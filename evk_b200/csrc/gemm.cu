@@ -40,10 +40,23 @@ constexpr uint32_t kTimeoutGemm = 0x101;
 
 // ------------------------------------------------- fused QKV epilogue ----
 // Inverse frequencies base^(-2p / Dh) for p < Dh / 2, once per CTA.
+__device__ __forceinline__ float rope_inv_freq(float base, uint32_t p, uint32_t Dh) {
+    return powf(base, -2.0f * (float)p / (float)Dh);
+}
+
 __device__ __forceinline__ void qkv_fill_inv_freq(const QkvRope& qr, float* inv_freq) {
     if (!qr.q) return;
-    for (uint32_t p = threadIdx.x; p < qr.Dh / 2; p += blockDim.x)
-        inv_freq[p] = powf(qr.base, -2.0f * (float)p / (float)qr.Dh);
+    for (uint32_t p = threadIdx.x; p < qr.Dh / 2; p += blockDim.x) inv_freq[p] = rope_inv_freq(qr.base, p, qr.Dh);
+}
+
+__global__ void rope_table_kernel(float2* __restrict__ cs, uint32_t len, uint32_t Dh, float base) {
+    const uint32_t half = Dh / 2;
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)len * half) return;
+    const uint32_t pos = (uint32_t)(i / half), p = (uint32_t)(i % half);
+    float sn, c;
+    sincosf((float)pos * rope_inv_freq(base, p, Dh), &sn, &c);
+    cs[i] = make_float2(c, sn);
 }
 
 // Destination of output (row, col) of the fused QKV projection (see QkvRope);
@@ -62,9 +75,15 @@ __device__ __forceinline__ T* qkv_dst(const QkvRope& qr, uint32_t pos_base, uint
 // Rotates the pair (x0, x1) = columns (2p, 2p + 1) of a q / k head.
 __device__ __forceinline__ void qkv_rotate(const QkvRope& qr, const float* inv_freq, uint32_t pos_base, uint32_t row,
                                            uint32_t col, float& x0, float& x1) {
-    const float t = (float)(pos_base + row % qr.S);
+    const uint32_t pos = pos_base + row % qr.S, p = (col % qr.Dh) >> 1;
     float sn, cs;
-    sincosf(t * inv_freq[(col % qr.Dh) >> 1], &sn, &cs);
+    if (qr.cs && pos < qr.cs_len) {
+        const float2 e = __ldg(qr.cs + (uint64_t)pos * (qr.Dh >> 1) + p);
+        cs = e.x;
+        sn = e.y;
+    } else {
+        sincosf((float)pos * inv_freq[p], &sn, &cs);
+    }
     const float a = x0 * cs - x1 * sn, b = x0 * sn + x1 * cs;
     x0 = a;
     x1 = b;
@@ -84,9 +103,10 @@ struct GemmCfg {
 
 template <typename T, int BN, bool A_MN, bool B_MN, int CPS>
 __global__ void __launch_bounds__(kGemmThreads, CPS)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, T* __restrict__ C,
-                   uint32_t M, uint32_t N, uint32_t K, uint64_t strideC, int bcastA, int bcastB, int acc_c,
-                   uint32_t idesc, unsigned int* err, int gelu, QkvRope qr) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, T* __restrict__ C, uint32_t M, uint32_t N, uint32_t K,
+                   uint64_t strideC, int bcastA, int bcastB, int acc_c, uint32_t idesc, unsigned int* err, int gelu,
+                   QkvRope qr, int tma_c) {
     using Cfg = GemmCfg<BN, CPS>;
     __shared__ float s_inv_freq[128];
     constexpr int STAGES = Cfg::STAGES;
@@ -97,7 +117,8 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * Cfg::STAGE_BYTES);
     uint64_t* empty = full + STAGES;
     uint64_t* accum = empty + STAGES;
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(accum + 1);
+    uint64_t* cbar = accum + 1;  // C tile loaded (acc_c with the TMA epilogue)
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(cbar + 1);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -129,10 +150,12 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
             mbar_init(&empty[s], 1);
         }
         mbar_init(accum, 1);
+        mbar_init(cbar, 1);
         *s_abort = 0;
         fence_barrier_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        if (tma_c) prefetch_tmap(&tmC);
     }
     if (warp == 1) {
         tmem_alloc(s_tmem, BN);
@@ -201,7 +224,67 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
                                     0) != 0;
         tc_fence_after();
         const uint32_t pos_base = qr.q ? (qr.d_pos ? *qr.d_pos : qr.pos0) : 0u;
-        if (ok) {
+        if (ok && tma_c) {
+            // Staged epilogue: the ring is idle once the accumulator is
+            // complete.  The C tile (acc_c) arrives there by TMA, each thread
+            // combines its row (TMEM lane) 32 columns at a time in place, and
+            // TMA stores write the tile back: coalesced global traffic instead
+            // of one 16-byte access per row per instruction.  The staging is
+            // BN / 64 boxes of 128 rows x 128 bytes in the 128-byte swizzle
+            // (16-byte chunk k of row r at chunk k ^ (r % 8)), so the eight
+            // rows of a quarter-warp hit eight different bank groups.
+            uint8_t* stg = smem;
+            const bool leader = warp == 2 && lane == 0;
+            bool go = true;
+            if (acc_c) {
+                if (leader) {
+                    mbar_arrive_expect_tx(cbar, (uint32_t)BN * BM * 2);
+#pragma unroll
+                    for (int j = 0; j < BN / 64; ++j)
+                        tma_load_3d(stg + j * (BM * 128), &tmC, cbar, (int)(n0 + 64 * j), (int)m0, (int)bz);
+                }
+                const bool got = __shfl_sync(0xffffffffu,
+                                             lane == 0 ? (int)mbar_wait(cbar, 0, s_abort, err, kTimeoutGemm) : 0, 0);
+                if (!got && leader) mbar_drain(cbar, 0);  // C loads land before the CTA may exit
+                go = got;
+            }
+            const uint32_t rr = q * 32 + lane;  // row within the tile
+#pragma unroll 1
+            for (int c = 0; go && c < BN / 32; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, r);
+                tmem_wait_ld();
+                uint8_t* box = stg + (c >> 1) * (BM * 128) + rr * 128;
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    const uint32_t kc = (uint32_t)((c & 1) * 4 + g);
+                    Vec8* p = reinterpret_cast<Vec8*>(box + ((kc ^ (rr & 7)) << 4));
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[g * 8 + e]);
+                    if (acc_c) {
+                        float o[8];
+                        unpack8<T>(ld_shared_vec8(p), o);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] += o[e];
+                    }
+                    if (gelu) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = gelu_f(f[e]);
+                    }
+                    st_shared_vec8(p, pack8<T>(f));
+                }
+            }
+            fence_proxy_async_smem();
+            named_barrier(1, 128);  // the four epilogue warps
+            if (leader && go) {
+#pragma unroll
+                for (int j = 0; j < BN / 64; ++j)
+                    tma_store_3d(&tmC, stg + j * (BM * 128), (int)(n0 + 64 * j), (int)m0, (int)bz);
+                tma_store_commit();
+                tma_store_wait_all();
+            }
+        } else if (ok) {
             const uint32_t row = m0 + q * 32 + lane;
             T* crow = C + (uint64_t)bz * strideC + (uint64_t)row * N;
 #pragma unroll 1
@@ -763,6 +846,18 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch
               uint64_t strideC, int bcastA, int bcastB, int acc, int is_bf16, int gelu, const QkvRope& qr,
               cudaStream_t st) {
     using Cfg = GemmCfg<BN, CPS>;
+    static_assert(Cfg::STAGES * Cfg::STAGE_BYTES >= BN * BM * 2, "C staging must fit in the ring");
+    // Staged (TMA) epilogue for plain C = A B (+ C) (GELU): a map of C with
+    // 64-column x 128-row boxes in the 128-byte swizzle.
+    CUtensorMap tc;
+    memset(&tc, 0, sizeof(tc));
+    int tma_c = 0;
+    if (!qr.q && !state()->plain_epilogue) {
+        const int r = make_tmap_3d(&tc, C, N, M, batch, N, batch > 1 ? strideC : (uint64_t)M * N, 64, BM,
+                                   is_bf16 ? EVKCU_BF16 : EVKCU_F16);
+        if (r) return r;
+        tma_c = 1;
+    }
     static bool attr_set = false;
     auto kern = gemm_tc_kernel<T, BN, A_MN, B_MN, CPS>;
     if (!attr_set) {
@@ -771,8 +866,8 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
     uint32_t idesc = make_idesc_f16(BM, BN, is_bf16, A_MN, B_MN);
-    kern<<<grid, kGemmThreads, Cfg::SMEM, st>>>(ta, tb, C, M, N, K, strideC, bcastA, bcastB, acc, idesc,
-                                                state()->d_error, gelu, qr);
+    kern<<<grid, kGemmThreads, Cfg::SMEM, st>>>(ta, tb, tc, C, M, N, K, strideC, bcastA, bcastB, acc, idesc,
+                                                state()->d_error, gelu, qr, tma_c);
     return after_launch("evkcu_matmul(tcgen05)");
 }
 
@@ -819,6 +914,13 @@ int launch_gemv(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32_t 
 using namespace evkcu;
 
 namespace evkcu {
+
+int rope_table(float2* cs, uint32_t len, uint32_t Dh, float base, cudaStream_t st) {
+    const uint64_t n = (uint64_t)len * (Dh / 2);
+    if (n == 0) return EVKCU_OK;
+    rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(cs, len, Dh, base);
+    return after_launch("rope table");
+}
 
 int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M, uint32_t K, uint32_t N,
               uint64_t stride_a, uint64_t stride_b, uint64_t stride_c, uint32_t flags, int dtype, int gelu,

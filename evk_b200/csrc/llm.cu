@@ -68,8 +68,8 @@ __global__ void fill_normal_kernel(T* dst, uint32_t rows, uint32_t cols, uint64_
 
 // After a decode step: one more cached position.
 __global__ void advance_kernel(uint32_t* d_pos, uint32_t* d_len) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     const uint32_t p = *d_pos + 1;
     *d_pos = p;
     d_pos[2] += 1;  // decode-step counter (never reset): all-reduce flag values
@@ -85,8 +85,8 @@ __global__ void set_pos_kernel(uint32_t* d_pos, uint32_t* d_len, uint32_t pos) {
 template <typename T>
 __global__ void argmax_key_kernel(const T* __restrict__ logits, uint32_t Vl, uint32_t voff,
                                   unsigned long long* __restrict__ keys) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     __shared__ unsigned long long sh[32];
     const T* row = logits + (uint64_t)blockIdx.x * Vl;
     unsigned long long best = 0;
@@ -115,8 +115,8 @@ __global__ void argmax_key_kernel(const T* __restrict__ logits, uint32_t Vl, uin
 // ids[b] = token of max_r keys[r * B + b] (token 0 when nothing is selectable).
 __global__ void keys_to_ids_kernel(const unsigned long long* __restrict__ keys, uint32_t ranks, uint32_t B,
                                    uint32_t* __restrict__ ids) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     const uint32_t b = blockIdx.x * blockDim.x + threadIdx.x;
     if (b >= B) return;
     unsigned long long best = 0;
@@ -145,6 +145,7 @@ struct evkcu_llm {
          *tmp = nullptr, *h1 = nullptr, *xl = nullptr, *logits = nullptr, *logits_all = nullptr;
     unsigned long long *keys = nullptr, *keys_all = nullptr;
     uint32_t *d_pos = nullptr, *d_len = nullptr, *d_epoch = nullptr;
+    float2* rope_cs = nullptr;  // (cos, sin) per position and rotation pair
     // Fused all-reduce of the decode Wo / W2 projections (tp > 1): this
     // rank's partial buffer and flags, and every rank's through IPC.
     float* ar_buf = nullptr;
@@ -226,6 +227,8 @@ int run_blocks(evkcu_llm* m, uint32_t B, uint32_t S, bool decode, cudaStream_t s
         qr.pos0 = 0;
         qr.d_pos = decode ? m->d_pos : nullptr;
         qr.base = c.rope_base;
+        qr.cs = m->rope_cs;
+        qr.cs_len = c.max_seq;
         LLM_TRY(matmul_ex(m->xn, L.wqkv, m->q /* not written */, 1, R, D, m->C, 0, 0, 0, 0, dt, 0, st, &qr));
         if (decode)
             LLM_TRY(evkcu_single_query_attention_devlen(m->q, L.kc, L.vc, m->attn, B, m->Hl, m->Hkvl, m->Dh,
@@ -452,6 +455,7 @@ extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_l
         A((void**)&m->keys_all, (size_t)c.max_batch * t * 8);
     }
     A((void**)&m->d_pos, 4 * sizeof(uint32_t));  // position, length, decode-step counter
+    A((void**)&m->rope_cs, (size_t)c.max_seq * (Dh / 2) * sizeof(float2));
     const uint32_t slabs = (uint32_t)((D + 127) / 128);
     if (t > 1) {
         A((void**)&m->ar_buf, (size_t)2 * t * 16 * D * sizeof(float));
@@ -469,6 +473,11 @@ extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_l
         const uint32_t init[4] = {0u, 0u, 1u, 0u};
         EVKCU_CUDA_TRY(cudaMemcpy(m->d_pos, init, sizeof(init), cudaMemcpyHostToDevice));
     }
+    if ((r = rope_table(m->rope_cs, c.max_seq, Dh, c.rope_base, 0)) != EVKCU_OK) {
+        evkcu_llm_destroy(m);
+        return r;
+    }
+    EVKCU_CUDA_TRY(cudaDeviceSynchronize());
     if (t > 1) setup_allreduce(m);  // falls back to NCCL when peer mappings are unavailable
     *out = m;
     return EVKCU_OK;

@@ -23,8 +23,8 @@ enum class Unary { Gelu, Scale };
 
 template <typename T, Unary OP>
 __global__ void unary_kernel(const T* __restrict__ in, T* __restrict__ out, uint64_t n, float s) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     uint64_t nvec = n / 8;
     uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -45,8 +45,8 @@ __global__ void unary_kernel(const T* __restrict__ in, T* __restrict__ out, uint
 
 template <typename T>
 __global__ void add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ c, uint64_t n) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     uint64_t nvec = n / 8;
     uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -68,16 +68,16 @@ __global__ void add_kernel(const T* __restrict__ a, const T* __restrict__ b, T* 
 // Scalar fallback for buffers that are not 16-byte aligned.
 template <typename T>
 __global__ void add_scalar_kernel(const T* a, const T* b, T* c, uint64_t n) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += stride)
         c[e] = Elem<T>::from_f(Elem<T>::to_f(a[e]) + Elem<T>::to_f(b[e]));
 }
 template <typename T, Unary OP>
 __global__ void unary_scalar_kernel(const T* in, T* out, uint64_t n, float s) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t e = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += stride) {
         float x = Elem<T>::to_f(in[e]);
@@ -88,8 +88,8 @@ __global__ void unary_scalar_kernel(const T* in, T* out, uint64_t n, float s) {
 // shaders/causal_mask.comp:16-33 — row-per-block so each thread only tests j > i.
 template <typename T>
 __global__ void causal_mask_kernel(T* __restrict__ scores, uint64_t rows, uint32_t N) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     const T sentinel = Elem<T>::from_f(-65504.0f);
     for (uint64_t r = blockIdx.x; r < rows; r += gridDim.x) {
         uint32_t i = (uint32_t)(r % N);
@@ -102,8 +102,8 @@ __global__ void causal_mask_kernel(T* __restrict__ scores, uint64_t rows, uint32
 template <typename T, typename I>
 __global__ void embed_kernel(const T* __restrict__ E, const I* __restrict__ idx, T* __restrict__ out,
                              uint32_t vocab, uint32_t dim, uint32_t n_idx, bool vec) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     for (uint32_t r = blockIdx.x; r < n_idx; r += gridDim.x) {
         uint32_t tok = (uint32_t)idx[r];
         if (tok >= vocab) tok = vocab - 1;

@@ -60,8 +60,8 @@ __device__ void block_max_sum(float& m, float& s, float* shm, float* shs) {
 template <typename T, bool VEC>
 __global__ void rms_norm_kernel(const T* __restrict__ in, T* __restrict__ out, const T* __restrict__ gamma,
                                 uint32_t D, float eps) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     __shared__ float sh[32];
     const uint64_t row = blockIdx.x;
     const T* x = in + row * D;
@@ -119,8 +119,8 @@ constexpr float kMaskSentinel = -65504.0f;
 
 template <typename T>
 __global__ void softmax_kernel(const T* __restrict__ in, T* __restrict__ out, uint32_t L, float scale, bool vec) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     __shared__ float shm[32], shs[32];
     const uint64_t row = blockIdx.x;
     const T* x = in + row * L;
@@ -171,8 +171,8 @@ __global__ void softmax_kernel(const T* __restrict__ in, T* __restrict__ out, ui
 template <typename T>
 __global__ void rope_kernel(const T* __restrict__ in, T* __restrict__ out, uint64_t rows, uint32_t seq_len,
                             uint32_t dim, uint32_t head_dim, uint32_t pos_offset, float base, bool vec) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     const uint32_t per_row = vec ? dim / 8 : dim / 2;  // work items per row
     const uint64_t total = rows * per_row;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;

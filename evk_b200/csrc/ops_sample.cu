@@ -55,8 +55,8 @@ __global__ void __launch_bounds__(kThreads) greedy_kernel(const T* __restrict__ 
                                                           uint32_t token_base, uint32_t token_count,
                                                           uint32_t out_bytes, uint64_t* __restrict__ partial,
                                                           unsigned int* __restrict__ tickets) {
-    pdl_wait();  // inputs come from earlier kernels (see launch_pdl)
-    pdl_trigger();
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
     __shared__ uint64_t sh[32];
     __shared__ bool is_last;
     const uint32_t b = blockIdx.y;
