@@ -224,7 +224,10 @@ __global__ void __launch_bounds__(kDecThreads) decode_attn_kernel(
 #pragma unroll
                 for (int j = 0; j < SB; ++j) {
                     float vf[8];
-                    if (dvalid) {
+                    // Rows at or past the length hold whatever the cache (or
+                    // the next sequence) has there: their weight is 0, and
+                    // their values must not enter o (0 * NaN = NaN).
+                    if (dvalid && pos0 + (jb + j) * KPW < pend) {
                         unpack8<T>(ld_shared_v4(vt + (r0 + (jb + j) * KPW) * Dh + d0), vf);
                     } else {
 #pragma unroll

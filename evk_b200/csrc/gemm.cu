@@ -104,7 +104,8 @@ struct GemmCfg {
 template <typename T, int BN, bool A_MN, bool B_MN, int CPS>
 __global__ void __launch_bounds__(kGemmThreads, CPS)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, T* __restrict__ C, uint32_t M, uint32_t N, uint32_t K,
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmKc,
+                   const __grid_constant__ CUtensorMap tmVc, T* __restrict__ C, uint32_t M, uint32_t N, uint32_t K,
                    uint64_t strideC, int bcastA, int bcastB, int acc_c, uint32_t idesc, unsigned int* err, int gelu,
                    QkvRope qr, int tma_c) {
     using Cfg = GemmCfg<BN, CPS>;
@@ -156,6 +157,10 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
         if (tma_c) prefetch_tmap(&tmC);
+        if (tma_c == 2) {
+            prefetch_tmap(&tmKc);
+            prefetch_tmap(&tmVc);
+        }
     }
     if (warp == 1) {
         tmem_alloc(s_tmem, BN);
@@ -233,6 +238,9 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
             // BN / 64 boxes of 128 rows x 128 bytes in the 128-byte swizzle
             // (16-byte chunk k of row r at chunk k ^ (r % 8)), so the eight
             // rows of a quarter-warp hit eight different bank groups.
+            // tma_c == 2 is the fused QKV epilogue of a prefill whose tiles
+            // each lie in one sequence: q and k are rotated in registers and
+            // every 64-column box goes to q, the K cache or the V cache.
             uint8_t* stg = smem;
             const bool leader = warp == 2 && lane == 0;
             bool go = true;
@@ -262,6 +270,14 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
                     float f[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[g * 8 + e]);
+                    if (tma_c == 2) {
+                        const uint32_t col = n0 + c * 32 + g * 8;
+                        if (col < (qr.Hq + qr.Hk) * qr.Dh) {
+#pragma unroll
+                            for (int e = 0; e < 8; e += 2)
+                                qkv_rotate(qr, s_inv_freq, pos_base, m0 + rr, col + e, f[e], f[e + 1]);
+                        }
+                    }
                     if (acc_c) {
                         float o[8];
                         unpack8<T>(ld_shared_vec8(p), o);
@@ -278,9 +294,22 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
             fence_proxy_async_smem();
             named_barrier(1, 128);  // the four epilogue warps
             if (leader && go) {
+                const uint32_t qcols = qr.Hq * qr.Dh, kcols = qr.Hk * qr.Dh;
 #pragma unroll
-                for (int j = 0; j < BN / 64; ++j)
-                    tma_store_3d(&tmC, stg + j * (BM * 128), (int)(n0 + 64 * j), (int)m0, (int)bz);
+                for (int j = 0; j < BN / 64; ++j) {
+                    const uint32_t col = n0 + 64 * j;
+                    if (tma_c != 2) {
+                        tma_store_3d(&tmC, stg + j * (BM * 128), (int)col, (int)m0, (int)bz);
+                    } else if (col < N) {
+                        const int pos = (int)(pos_base + m0 % qr.S), b = (int)(m0 / qr.S);
+                        if (col < qcols)
+                            tma_store_3d(&tmC, stg + j * (BM * 128), (int)col, (int)m0, 0);
+                        else if (col < qcols + kcols)
+                            tma_store_3d(&tmKc, stg + j * (BM * 128), (int)(col - qcols), pos, b);
+                        else
+                            tma_store_3d(&tmVc, stg + j * (BM * 128), (int)(col - qcols - kcols), pos, b);
+                    }
+                }
                 tma_store_commit();
                 tma_store_wait_all();
             }
@@ -849,14 +878,25 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch
     static_assert(Cfg::STAGES * Cfg::STAGE_BYTES >= BN * BM * 2, "C staging must fit in the ring");
     // Staged (TMA) epilogue for plain C = A B (+ C) (GELU): a map of C with
     // 64-column x 128-row boxes in the 128-byte swizzle.
-    CUtensorMap tc;
+    CUtensorMap tc, tk, tv;
     memset(&tc, 0, sizeof(tc));
+    memset(&tk, 0, sizeof(tk));
+    memset(&tv, 0, sizeof(tv));
+    const int dt = is_bf16 ? EVKCU_BF16 : EVKCU_F16;
     int tma_c = 0;
     if (!qr.q && !state()->plain_epilogue) {
-        const int r = make_tmap_3d(&tc, C, N, M, batch, N, batch > 1 ? strideC : (uint64_t)M * N, 64, BM,
-                                   is_bf16 ? EVKCU_BF16 : EVKCU_F16);
+        const int r = make_tmap_3d(&tc, C, N, M, batch, N, batch > 1 ? strideC : (uint64_t)M * N, 64, BM, dt);
         if (r) return r;
         tma_c = 1;
+    } else if (qr.q && !qr.d_pos && qr.S % BM == 0 && (qr.Hq * qr.Dh) % 64 == 0 && (qr.Hk * qr.Dh) % 64 == 0 &&
+               batch == 1 && !state()->plain_epilogue) {
+        // Fused QKV of a prefill: q [M, Hq * Dh]; caches [M / S, max_len, Hk * Dh].
+        const uint64_t qc = (uint64_t)qr.Hq * qr.Dh, kc = (uint64_t)qr.Hk * qr.Dh, nb = M / qr.S;
+        int r = make_tmap_3d(&tc, qr.q, qc, M, 1, qc, qc * M, 64, BM, dt);
+        if (!r) r = make_tmap_3d(&tk, qr.kc, kc, qr.max_len, nb, kc, kc * qr.max_len, 64, BM, dt);
+        if (!r) r = make_tmap_3d(&tv, qr.vc, kc, qr.max_len, nb, kc, kc * qr.max_len, 64, BM, dt);
+        if (r) return r;
+        tma_c = 2;
     }
     static bool attr_set = false;
     auto kern = gemm_tc_kernel<T, BN, A_MN, B_MN, CPS>;
@@ -866,7 +906,7 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch
     }
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
     uint32_t idesc = make_idesc_f16(BM, BN, is_bf16, A_MN, B_MN);
-    kern<<<grid, kGemmThreads, Cfg::SMEM, st>>>(ta, tb, tc, C, M, N, K, strideC, bcastA, bcastB, acc, idesc,
+    kern<<<grid, kGemmThreads, Cfg::SMEM, st>>>(ta, tb, tc, tk, tv, C, M, N, K, strideC, bcastA, bcastB, acc, idesc,
                                                 state()->d_error, gelu, qr, tma_c);
     return after_launch("evkcu_matmul(tcgen05)");
 }

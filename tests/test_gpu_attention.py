@@ -165,3 +165,25 @@ def test_single_query_attention_scratch_reuse_across_shapes():
         r = np.empty(B * H * Dh, np.uint16)
         oracle.single_query_attention(q, kc, vc, r, B, H, H, Dh, L, cur)
         assert_close(u16(out).ravel(), r, 0, what=f"decode reuse {(B, H, Dh, L, cur)}")
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_single_query_attention_ignores_cache_rows_past_length(dtype):
+    """Rows at and past cur_len (a cache's unwritten tail, or the next
+    sequence's rows inside the same 64-row tile) carry weight 0: NaN / Inf
+    there must not reach the output (0 * NaN would)."""
+    B, H, Dh, L, cur = 2, 4, 64, 160, 131
+    dc = dcode(dtype)
+    q = oracle.normal(B * H * Dh, 61, dtype=dc)
+    kc = oracle.normal(B * L * H * Dh, 62, dtype=dc).reshape(B, L, H * Dh)
+    vc = oracle.normal(B * L * H * Dh, 63, dtype=dc).reshape(B, L, H * Dh)
+    r = np.empty(B * H * Dh, np.uint16)
+    oracle.single_query_attention(q, kc.ravel().copy(), vc.ravel().copy(), r, B, H, H, Dh, L, cur, 0.0, dc)
+    nan = 0x7E00 if dc == 0 else 0x7FC0
+    kc[:, cur:, :] = nan
+    vc[:, cur:, :] = nan
+    out = torch.empty(B, H * Dh, dtype=dtype, device="cuda")
+    ev().single_query_attention(dev(q, dtype).view(B, H * Dh), dev(kc.ravel(), dtype).view(B, L, H * Dh),
+                                dev(vc.ravel(), dtype).view(B, L, H * Dh), out, H, cur)
+    assert bool(torch.isfinite(out.float()).all())
+    assert_close(u16(out).ravel(), r, dc, rel_l2=1e-3 if dc == 0 else 4e-3, what="decode with NaN tail")

@@ -32,6 +32,9 @@ def build(tied, dtype, layers=2, D=256, H=4, F=512, V=1000, max_batch=2, max_seq
     for l, w in enumerate(ref.w):
         for n in ("wqkv", "wo", "w1", "w2"):
             m.set_weight(n, dev(w[n], tdt), layer=l)
+    # set_weight copies on the default stream; the tests then run on their
+    # own (non-blocking) streams.
+    torch.cuda.synchronize()
     return ref, m, tdt
 
 
@@ -161,3 +164,34 @@ def test_llm_fused_head_argmax_matches_logits_path(tied):
         runs.append(torch.stack(ids).cpu().numpy())
         m.close()
     assert np.array_equal(runs[0], runs[1]), (runs[0], runs[1])
+
+
+@pytest.mark.parametrize("dtype", [0, 1])
+def test_llm_tile_aligned_prefill_vs_oracle(dtype):
+    """A prompt of 128 tokens puts every 128-row GEMM tile inside one sequence,
+    so the fused QKV projection takes the staged (TMA) epilogue that stores
+    q and the K / V cache rows by tile; prefill and the decode steps that read
+    that cache must still match the oracle."""
+    ref, m, tdt = build(False, dtype, max_seq=160)
+    B, S, steps = 2, 128, 3
+    prompt = np.random.default_rng(12).integers(0, ref.V, size=(B, S)).astype(np.int32)
+    nxt = torch.zeros(B, dtype=torch.int32, device="cuda")
+    logits = torch.empty(B, ref.V, dtype=tdt, device="cuda")
+    stream = torch.cuda.Stream()
+    stats = {"checked": 0, "close_calls": 0}
+    with torch.cuda.stream(stream):
+        m.prefill(torch.from_numpy(prompt).cuda(), nxt, logits, stream=stream)
+    torch.cuda.synchronize()
+    seq = prompt.copy()
+    check_step(ref, seq, logits, nxt.cpu().numpy(), dtype, stats)
+    cur = nxt.clone()
+    for _ in range(steps):
+        seq = np.concatenate([seq, cur.cpu().numpy().reshape(B, 1)], axis=1)
+        out = torch.zeros(B, dtype=torch.int32, device="cuda")
+        with torch.cuda.stream(stream):
+            m.decode(cur, out, logits, stream=stream)
+        torch.cuda.synchronize()
+        check_step(ref, seq, logits, out.cpu().numpy(), dtype, stats)
+        cur = out
+    assert stats["close_calls"] <= 1, stats
+    m.close()
