@@ -34,13 +34,17 @@ constexpr uint32_t kTimeoutFlash = 0x201;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
 // NT query tiles per CTA, each with its own softmax warpgroup, share every
-// K/V block.  Dh = 64 runs NT = 2 (two warpgroups ping-pong on the tensor
-// core); Dh = 128 runs NT = 1 to fit shared memory.
+// K/V block: while one tile's softmax runs, the tensor core works on the
+// other's S or PV.
 template <int DH, int NT>
 struct FlashCfg {
     static constexpr int Q_BYTES = FM * DH * 2;  // per tile
     static constexpr int KV_BYTES = FN * DH * 2;  // one K or V block
-    static constexpr int STAGES = NT == 2 ? 5 : (DH == 64 ? 6 : 3);
+    static constexpr int STAGES = NT == 2 ? (DH == 64 ? 5 : 2) : (DH == 64 ? 6 : 3);
+    // Dh = 128 with two tiles: S (128) + O (128) columns per tile fill TMEM,
+    // so P (16-bit pairs, 64 columns) is written over the tile's S, and
+    // S_t(j + 1) waits until PV_t(j) has read it.
+    static constexpr bool ALIAS_P = DH == 128 && NT == 2;
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
     static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
@@ -52,9 +56,11 @@ struct FlashCfg {
     // values packed two per column, FN/2 columns).
     static __device__ __forceinline__ uint32_t col_s(int t) { return t * 256; }
     static __device__ __forceinline__ uint32_t col_o(int t) { return t * 256 + FN; }
-    static __device__ __forceinline__ uint32_t col_p(int t) { return NT == 2 ? t * 256 + FN + DH : FN + DH; }
+    static __device__ __forceinline__ uint32_t col_p(int t) {
+        return ALIAS_P ? t * 256 : (NT == 2 ? t * 256 + FN + DH : FN + DH);
+    }
 };
-static_assert(FlashCfg<64, 2>::SMEM <= 227 * 1024 && FlashCfg<128, 1>::SMEM <= 227 * 1024, "flash smem");
+static_assert(FlashCfg<64, 2>::SMEM <= 227 * 1024 && FlashCfg<128, 2>::SMEM <= 227 * 1024, "flash smem");
 
 // max(a, b, c) in one instruction (sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -252,6 +258,7 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
         // each issuer (kv_empty counts 2).
         const bool is_s = warp == 1;
         const bool leader = elect_one();
+        uint64_t* const s_reuse = Cfg::ALIAS_P ? pv_done : s_free;  // S_t(j) waits on this for j - 1
         const uint32_t qaddr = smem_u32(sQ);
         uint32_t rbase = 0, it = 0;
         uint32_t gs[NT], ep[NT];  // per tile: blocks processed before this item, epilogues finished
@@ -278,7 +285,10 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
                     for (int t = 0; t < NT; ++t) {
                         const uint32_t gj = gs[t] + j;  // tile-global block index
                         if (!ok || j >= nblk[t]) continue;
-                        ok = gj == 0 || probe(lane == 0 && mbar_wait(&s_free[t], (gj - 1) & 1, s_abort, err,
+                        // S_t(j) overwrites S_t(j - 1): softmax t must have
+                        // read it, and with P aliased into S, PV_t(j - 1)
+                        // must have read P (which also implies the former).
+                        ok = gj == 0 || probe(lane == 0 && mbar_wait(&s_reuse[t], (gj - 1) & 1, s_abort, err,
                                                                      kTimeoutFlash));
                         if (!ok) break;
                         tc_fence_after();
@@ -609,7 +619,7 @@ int flash_attention_kv_strided(const void* q, const void* k, const void* v, void
         return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
             if (Dh == 64)
                 return launch_flash_tc<T, 64, 2>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, kv_bstride, st);
-            return launch_flash_tc<T, 128, 1>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, kv_bstride, st);
+            return launch_flash_tc<T, 128, 2>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, kv_bstride, st);
         });
     }
     const uint64_t warps = (uint64_t)B * H * N;
