@@ -289,6 +289,43 @@ def profile_leg(leg):
     evk.check_device_error()
 
 
+# Projection GEMM shapes of the LLM configs' prefill (bf16, M = batch x prompt
+# rows), with the residual add (C +=) where the driver fuses it.
+GEMM_SHAPES = [("C4 QKV", 16384, 2048, 6144, False), ("C4 Wo", 16384, 2048, 2048, True),
+               ("C4 W1", 16384, 2048, 8192, False), ("C4 W2", 16384, 8192, 2048, True),
+               ("8192^3", 8192, 8192, 8192, False), ("C5 QKV", 65536, 4096, 12288, False),
+               ("C5 Wo", 65536, 4096, 4096, True)]
+
+
+def gemm_shapes():
+    """TFLOP/s of evkcu_matmul on the prefill projection shapes (CUDA events,
+    10 launches after 3 warm-up, inputs resident).  EVKCU_GEMM_PLAIN_EPILOGUE=1
+    selects the per-row-store epilogue for comparison."""
+    import torch
+
+    import evk_b200 as evk
+
+    evk.init(0)
+    for name, M, K, N, acc in GEMM_SHAPES:
+        a = torch.randn(M, K, device="cuda").bfloat16()
+        b = (torch.randn(K, N, device="cuda") * 0.02).bfloat16()
+        c = torch.zeros(M, N, device="cuda").bfloat16()
+        for _ in range(3):
+            evk.matmul(a, b, c, acc_c=acc)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(10):
+            evk.matmul(a, b, c, acc_c=acc)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 10
+        print(json.dumps({"shape": name, "M": M, "K": K, "N": N, "acc_c": acc, "us": round(ms * 1e3, 1),
+                          "tflops": round(2.0 * M * N * K / ms / 1e9, 1)}), flush=True)
+        del a, b, c
+    evk.check_device_error()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -299,12 +336,16 @@ def main():
     ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--profile-leg", choices=["flash", "gemm", "gemv", "decode"], default=None,
                     help="run a few launches of one leg and exit (for ncu captures; prints no JSON)")
+    ap.add_argument("--gemm-shapes", action="store_true",
+                    help="print TFLOP/s of the prefill projection GEMM shapes (one JSON line each) and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
     if args.profile_leg:
         return profile_leg(args.profile_leg)
+    if args.gemm_shapes:
+        return gemm_shapes()
 
     import torch
 
