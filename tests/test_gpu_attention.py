@@ -61,6 +61,30 @@ def test_flash_vs_oracle(dtype, case):
     assert_close(u16(to).ravel(), r, dc, max_abs=2e-2, rel_l2=rel, what=f"flash {case}")
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("causal", [True, False])
+def test_flash_scores_growing_along_the_sequence(dtype, causal):
+    """Scores that grow linearly with the key position (k proportional to the
+    position): every 128-key block's maximum exceeds the previous one by ~17
+    in log2 units, so the lazily kept reference maximum of every row must move
+    (and O be rescaled) on every block."""
+    B, N, H, Dh = 1, 512, 2, 64
+    dc = dcode(dtype)
+    pos = np.arange(N, dtype=np.float32)
+    qf = np.full((B, N, H, Dh), 0.5, np.float32)
+    kf = np.repeat((3.0 * pos / 128.0)[None, :, None, None], H, axis=2) * np.ones((B, N, H, Dh), np.float32)
+    q = oracle.from_float(qf.ravel(), dc)
+    k = oracle.from_float(kf.ravel(), dc)
+    v = oracle.normal(B * N * H * Dh, 71, dtype=dc)
+    to = torch.empty(B, N, H * Dh, dtype=dtype, device="cuda")
+    ev().flash_attention(dev(q, dtype).view(B, N, H * Dh), dev(k, dtype).view(B, N, H * Dh),
+                         dev(v, dtype).view(B, N, H * Dh), to, heads=H, causal=causal)
+    r = np.empty_like(q)
+    oracle.flash_attention(q, k, v, r, B, N, H, H, Dh, 0.0, int(causal), dc)
+    assert bool(torch.isfinite(to.float()).all())
+    assert_close(u16(to).ravel(), r, dc, max_abs=2e-2, rel_l2=1e-3 if dc == 0 else 8e-3, what="flash growing scores")
+
+
 def test_flash_reference_api_default_mqa():
     """evk::ai::flash_attention call shape: K/V (B, N, Dh) shared by all heads."""
     B, N, H, Dh = 2, 256, 4, 64
