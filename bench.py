@@ -277,7 +277,22 @@ def profile_leg(leg):
         y = torch.empty(16, 14336, device="cuda").bfloat16()
         for _ in range(3):
             evk.matmul(x, w, y)
-    else:
+    elif leg == "llm-decode":
+        # C4 (random weights): one prefill, then four eager decode steps (the
+        # launch list of one step is the last quarter of the decode launches).
+        L, D, Hh, F, V, Bb, Sp, _, dt, tied = LLM_CONFIGS["C4_1.3B"]
+        m = evk.Llm(L, D, Hh, F, V, Bb, Sp + 16, dtype=dt, tied_embeddings=tied)
+        m.init_random(42, 0.02)
+        tok = torch.randint(0, V, (Bb, Sp), dtype=torch.int32, device="cuda")
+        nxt = torch.zeros(Bb, dtype=torch.int32, device="cuda")
+        m.prefill(tok, nxt)
+        cur, out = nxt.clone(), torch.zeros_like(nxt)
+        for _ in range(4):
+            m.decode(cur, out)
+            cur, out = out, cur
+        torch.cuda.synchronize()
+        m.close()
+    elif leg == "decode":
         # C4 decode attention: B=8, H=16, Dh=128 over 2048 cached positions (bf16)
         q = torch.randn(8, 16 * 128, device="cuda").bfloat16()
         kc = torch.randn(8, 2048, 16 * 128, device="cuda").bfloat16()
@@ -334,7 +349,7 @@ def main():
     ap.add_argument("--impl", default="evk_b200", choices=["evk_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true")
-    ap.add_argument("--profile-leg", choices=["flash", "gemm", "gemv", "decode"], default=None,
+    ap.add_argument("--profile-leg", choices=["flash", "gemm", "gemv", "decode", "llm-decode"], default=None,
                     help="run a few launches of one leg and exit (for ncu captures; prints no JSON)")
     ap.add_argument("--gemm-shapes", action="store_true",
                     help="print TFLOP/s of the prefill projection GEMM shapes (one JSON line each) and exit")
