@@ -111,6 +111,60 @@ __global__ void rms_norm_kernel(const T* __restrict__ in, T* __restrict__ out, c
     }
 }
 
+// One warp per row (up to 8 * 32 * NV elements): the row stays in registers
+// as packed 16-byte vectors between the sum of squares and the output, so it
+// is read once and the reduction is warp shuffles only.  Eight rows per
+// 256-thread CTA; used for many rows (prefill), where it streams faster than
+// one CTA per row.
+template <typename T, int NV>
+__global__ void __launch_bounds__(256) rms_norm_warp_kernel(const T* __restrict__ in, T* __restrict__ out,
+                                                            const T* __restrict__ gamma, uint32_t rows, uint32_t D,
+                                                            float eps) {
+    pdl_trigger();  // the next kernel may launch and run its prologue now
+    pdl_wait();     // inputs come from earlier kernels (see launch_pdl)
+    const uint32_t row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const uint32_t lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const Vec8* xv = reinterpret_cast<const Vec8*>(in + (uint64_t)row * D);
+    const uint32_t nv = D / 8;
+    Vec8 v[NV];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const uint32_t c = lane + 32u * i;
+        if (c < nv) {
+            v[i] = xv[c];
+            float f[8];
+            unpack8<T>(v[i], f);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float x = fminf(fmaxf(f[k], -65504.0f), 65504.0f);
+                ss += x * x;
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float inv = rsqrtf(ss / (float)D + eps);
+    const Vec8* gv = reinterpret_cast<const Vec8*>(gamma);
+    Vec8* yv = reinterpret_cast<Vec8*>(out + (uint64_t)row * D);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const uint32_t c = lane + 32u * i;
+        if (c < nv) {
+            float f[8], g[8];
+            unpack8<T>(v[i], f);
+            if (gamma) unpack8<T>(gv[c], g);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float x = fminf(fmaxf(f[k], -65504.0f), 65504.0f) * inv;
+                f[k] = gamma ? x * g[k] : x;
+            }
+            yv[c] = pack8<T>(f);
+        }
+    }
+}
+
 // ----------------------------------------------------------------- softmax --
 // shaders/softmax.comp:23-66: entries with raw <= -65504 are masked (skipped
 // in max and sum, written as 0); sum clamped to >= 1e-20; outputs computed
@@ -229,7 +283,22 @@ extern "C" int evkcu_rms_norm(const void* in, void* out, const void* gamma, uint
     EVKCU_CHECK_ARG(D > 0, EVKCU_BAD_SHAPE, "evkcu_rms_norm: D must be > 0");
     bool vec = (D % 8 == 0) && aligned16(in) && aligned16(out) && (!gamma || aligned16(gamma));
     unsigned threads = row_threads(vec ? D / 8 : D);
+    const uint32_t per_lane = (D / 8 + 31) / 32;  // 16-byte vectors per lane, one warp per row
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
+        // Many rows: one warp per row (measured 36.8 -> 28.0 us at 16384 x 2048);
+        // a few rows (decode) keep one CTA per row, which spreads them over SMs.
+        if (vec && per_lane <= 16 && rows >= 256) {
+            const unsigned grid = (rows + 7) / 8;
+            auto go = [&](auto kern) {
+                return launch_pdl("evkcu_rms_norm", kern, grid, 256, 0, as_stream(stream), (const T*)in, (T*)out,
+                                  (const T*)gamma, rows, D, eps);
+            };
+            if (per_lane <= 1) return go(rms_norm_warp_kernel<T, 1>);
+            if (per_lane <= 2) return go(rms_norm_warp_kernel<T, 2>);
+            if (per_lane <= 4) return go(rms_norm_warp_kernel<T, 4>);
+            if (per_lane <= 8) return go(rms_norm_warp_kernel<T, 8>);
+            return go(rms_norm_warp_kernel<T, 16>);
+        }
         if (vec)
             return launch_pdl("evkcu_rms_norm", rms_norm_kernel<T, true>, rows, threads, 0, as_stream(stream),
                               (const T*)in, (T*)out, (const T*)gamma, D, eps);

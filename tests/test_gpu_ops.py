@@ -107,7 +107,7 @@ def test_add_gelu_scale(dtype, n):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("rows,D", [(1, 512), (5, 4), (33, 2048), (7, 100), (4, 4096)])
+@pytest.mark.parametrize("rows,D", [(1, 512), (5, 4), (33, 2048), (7, 100), (4, 4096), (300, 2048), (259, 4096), (256, 24)])
 def test_rms_norm(dtype, rows, D):
     dc = dcode(dtype)
     x = oracle.normal(rows * D, 3, 3.0, dtype=dc)
