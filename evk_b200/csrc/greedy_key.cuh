@@ -6,7 +6,8 @@
 // its winner among lanes holding the global maximum is the lane with the
 // smallest bit-reversed index, and within a lane the smallest j.  The key
 //     hi32 = order-preserving bits of the value (0 for NaN and -inf, which the
-//            reference never selects since `v > -FLT_MAX` is false)
+//            reference never selects since `v > -FLT_MAX` is false; -0.0
+//            keys as +0.0, since `>` treats the two zeros as equal)
 //     lo32 = ~(bitrev8(j & 255) << 24 | (j >> 8))
 // makes that winner the maximum key, so any reduction order (split CTAs,
 // tensor-parallel vocabulary shards) selects the reference's token.
@@ -18,6 +19,7 @@ namespace evkcu {
 
 __device__ __forceinline__ uint64_t elem_key(float v, uint32_t j) {
     if (!(v > -FLT_MAX)) return 0ull;  // NaN, -inf: never selected
+    if (v == 0.0f) v = 0.0f;           // -0.0 ties with +0.0
     uint32_t u = __float_as_uint(v);
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
     uint32_t rank = (__brev(j & 255u) >> 24) << 24 | (j >> 8);

@@ -344,30 +344,30 @@ extern "C" int evkcu_comm_destroy(void* comm) {
 }
 
 // Exchanges CUDA IPC handles of every rank's all-reduce buffer and flags
-// (ncclAllGather of the 2 x 64-byte handles) and maps the peers' into this
-// process.  Leaves ar_ready false (NCCL all-reduce path) on any failure.
-static void setup_allreduce(evkcu_llm* m) {
+// (ncclAllGather of the 2 x 64-byte handles), maps the peers' into this
+// process, then agrees across ranks (ncclAllReduce, min) on whether every rank
+// succeeded and has the fused path switched on.  Every rank issues the same
+// two collectives whatever happens locally, so a failure on one rank (or
+// EVKCU_DISABLE_FUSED_ALLREDUCE set on some ranks only) makes all of them keep
+// the NCCL all-reduce instead of one rank waiting for peers that never arrive.
+// `xch` is a device buffer of 128 * (t + 1) + 4 bytes allocated by the caller.
+static void setup_allreduce(evkcu_llm* m, char* xch) {
     const uint32_t t = m->cfg.tp_size, rank = m->cfg.tp_rank;
-    if (t > 8 || !m->ar_buf || !m->ar_flags) return;
+    if (t > 8) return;  // same decision on every rank: t is shared
+    bool ok = m->ar_buf && m->ar_flags && getenv("EVKCU_DISABLE_FUSED_ALLREDUCE") == nullptr;
     const size_t fbytes = (size_t)2 * m->cfg.layers * ((m->cfg.d_model + 127) / 128) * t * sizeof(uint32_t);
-    if (cudaMemset(m->ar_flags, 0, fbytes) != cudaSuccess) return;
+    ok = ok && cudaMemset(m->ar_flags, 0, fbytes) == cudaSuccess;
     cudaIpcMemHandle_t h[2];
-    if (cudaIpcGetMemHandle(&h[0], m->ar_buf) != cudaSuccess || cudaIpcGetMemHandle(&h[1], m->ar_flags) != cudaSuccess) {
-        cudaGetLastError();
-        return;
-    }
-    char* d = nullptr;
-    if (cudaMalloc(&d, sizeof(h) * (t + 1)) != cudaSuccess) return;
+    std::memset(h, 0, sizeof(h));
+    ok = ok && cudaIpcGetMemHandle(&h[0], m->ar_buf) == cudaSuccess &&
+         cudaIpcGetMemHandle(&h[1], m->ar_flags) == cudaSuccess;
+    cudaGetLastError();
     std::vector<cudaIpcMemHandle_t> all(2 * t);
-    bool ok = cudaMemcpy(d, h, sizeof(h), cudaMemcpyHostToDevice) == cudaSuccess &&
-              ncclAllGather(d, d + sizeof(h), sizeof(h), ncclUint8, m->comm, 0) == ncclSuccess &&
-              cudaStreamSynchronize(0) == cudaSuccess &&
-              cudaMemcpy(all.data(), d + sizeof(h), sizeof(h) * t, cudaMemcpyDeviceToHost) == cudaSuccess;
-    cudaFree(d);
-    if (!ok) {
-        cudaGetLastError();
-        return;
-    }
+    bool comm_ok = cudaMemcpy(xch, h, sizeof(h), cudaMemcpyHostToDevice) == cudaSuccess &&
+                   ncclAllGather(xch, xch + sizeof(h), sizeof(h), ncclUint8, m->comm, 0) == ncclSuccess &&
+                   cudaStreamSynchronize(0) == cudaSuccess &&
+                   cudaMemcpy(all.data(), xch + sizeof(h), sizeof(h) * t, cudaMemcpyDeviceToHost) == cudaSuccess;
+    ok = ok && comm_ok;
     GemvAllReduce ar;
     ar.tp = t;
     ar.rank = rank;
@@ -386,14 +386,20 @@ static void setup_allreduce(evkcu_llm* m) {
         ar.buf[q] = (float*)pb;
         ar.flags[q] = (uint32_t*)pf;
     }
-    if (!ok) {
+    cudaGetLastError();
+    // Agreement: the fused path is used only if it is ready on every rank.
+    int32_t* flag = (int32_t*)(xch + sizeof(h) * (t + 1));
+    const int32_t mine = ok ? 1 : 0;
+    int32_t agreed = 0;
+    if (!(cudaMemcpy(flag, &mine, 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+          ncclAllReduce(flag, flag, 1, ncclInt32, ncclMin, m->comm, 0) == ncclSuccess &&
+          cudaStreamSynchronize(0) == cudaSuccess &&
+          cudaMemcpy(&agreed, flag, 4, cudaMemcpyDeviceToHost) == cudaSuccess)) {
         cudaGetLastError();
-        return;
+        agreed = 0;
     }
     m->ar = ar;
-    // Enabled where it has been validated on the GPU (two ranks); other sizes
-    // keep the NCCL all-reduce.
-    m->ar_ready = t == 2 && getenv("EVKCU_DISABLE_FUSED_ALLREDUCE") == nullptr;
+    m->ar_ready = agreed == 1;
 }
 
 extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_llm** out) {
@@ -457,7 +463,9 @@ extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_l
     A((void**)&m->d_pos, 4 * sizeof(uint32_t));  // position, length, decode-step counter
     A((void**)&m->rope_cs, (size_t)c.max_seq * (Dh / 2) * sizeof(float2));
     const uint32_t slabs = (uint32_t)((D + 127) / 128);
+    char* xch = nullptr;  // handle exchange / agreement word of setup_allreduce
     if (t > 1) {
+        A((void**)&xch, (size_t)128 * (t + 1) + 4);
         A((void**)&m->ar_buf, (size_t)2 * t * 16 * D * sizeof(float));
         A((void**)&m->ar_flags, (size_t)2 * c.layers * slabs * t * sizeof(uint32_t));
     }
@@ -478,7 +486,7 @@ extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_l
         return r;
     }
     EVKCU_CUDA_TRY(cudaDeviceSynchronize());
-    if (t > 1) setup_allreduce(m);  // falls back to NCCL when peer mappings are unavailable
+    if (t > 1) setup_allreduce(m, xch);  // all ranks fall back to NCCL unless every rank mapped its peers
     *out = m;
     return EVKCU_OK;
 }

@@ -154,32 +154,44 @@ int oracle_num_threads(void) { return n_threads(); }
 void oracle_matmul(const uint16_t* A, const uint16_t* B, uint16_t* C, uint32_t batch, uint32_t M, uint32_t K,
                    uint32_t N, uint64_t stride_a, uint64_t stride_b, uint64_t stride_c, uint32_t flags, int dt) {
     const bool ta = flags & 1u, tb = flags & 2u, acc = flags & 4u;
-    par_for((int64_t)batch * M, [&](int64_t bm) {
+    // Rows are independent; with few rows (decode shapes) each row is also
+    // split into column chunks so every thread has work.  The chunking does
+    // not change any element's summation order.
+    const int64_t rows = (int64_t)batch * M;
+    int64_t chunks = 1;
+    if (rows < 4 * n_threads()) chunks = std::min<int64_t>((4 * n_threads() + rows - 1) / rows, (N + 255) / 256);
+    if (chunks < 1) chunks = 1;
+    const uint32_t cw = (uint32_t)((N + chunks - 1) / chunks);
+    par_for(rows * chunks, [&](int64_t task) {
         {
+            const int64_t bm = task / chunks, ch = task % chunks;
             const int64_t b = bm / M, m = bm % M;
+            const uint32_t n0 = (uint32_t)std::min<int64_t>((int64_t)ch * cw, N);
+            const uint32_t n1 = (uint32_t)std::min<int64_t>((int64_t)n0 + cw, N);
+            if (n0 >= n1) return;
             const uint16_t* a = A + b * stride_a;
             const uint16_t* bb = B + b * stride_b;
             uint16_t* c = C + b * stride_c;
             std::vector<float> arow(K);
             for (uint32_t k = 0; k < K; ++k) arow[k] = ld(a, ta ? (uint64_t)k * M + m : (uint64_t)m * K + k, dt);
-            std::vector<double> acc_row(N, 0.0);
+            std::vector<double> acc_row(n1 - n0, 0.0);
             if (!tb) {
                 for (uint32_t k = 0; k < K; ++k) {
                     const double av = arow[k];
                     if (av == 0.0) continue;
                     const uint16_t* brow = bb + (uint64_t)k * N;
-                    for (uint32_t n = 0; n < N; ++n) acc_row[n] += av * (double)ld(brow, n, dt);
+                    for (uint32_t n = n0; n < n1; ++n) acc_row[n - n0] += av * (double)ld(brow, n, dt);
                 }
             } else {
-                for (uint32_t n = 0; n < N; ++n) {
+                for (uint32_t n = n0; n < n1; ++n) {
                     const uint16_t* brow = bb + (uint64_t)n * K;
                     double s = 0.0;
                     for (uint32_t k = 0; k < K; ++k) s += (double)arow[k] * (double)ld(brow, k, dt);
-                    acc_row[n] = s;
+                    acc_row[n - n0] = s;
                 }
             }
-            for (uint32_t n = 0; n < N; ++n) {
-                double v = acc_row[n];
+            for (uint32_t n = n0; n < n1; ++n) {
+                double v = acc_row[n - n0];
                 if (acc) v += (double)ld(c, (uint64_t)m * N + n, dt);
                 c[(uint64_t)m * N + n] = st((float)v, dt);
             }

@@ -114,7 +114,7 @@ def test_flash_full_size_c2_vs_torch(dtype):
     err = (o.float() - ref)
     rel = (err.norm() / ref.norm()).item()
     assert rel <= (1e-3 if dtype == torch.float16 else 8e-3), rel
-    assert err.abs().max().item() <= 2e-2 if dtype == torch.float16 else 6e-2
+    assert err.abs().max().item() <= (2e-2 if dtype == torch.float16 else 6e-2)
 
 
 def test_reference_flash_vs_unfused_n32768():

@@ -134,36 +134,23 @@ def test_llm_random_init_is_deterministic():
 
 
 @pytest.mark.parametrize("tied", [True, False])
-def test_llm_fused_head_argmax_matches_logits_path(tied):
+def test_llm_fused_head_argmax_vs_oracle(tied):
     """Without logits the LM-head GEMV reduces its outputs to greedy keys
-    (fused argmax); the ids must equal those of the logits + greedy_sample
-    path bit for bit, prefill and decode."""
+    (fused argmax).  Its ids must equal the logits + greedy_sample path's bit
+    for bit, and the oracle's greedy ids (teacher-forced, gap rule of
+    tests/llm_parity.py), prefill and decode."""
     import evk_b200
+    from llm_parity import load_weights, teacher_forced_parity
 
     evk_b200.init(0)
     V = 4000  # 32 slabs of 128 columns, a ragged last one
-    runs = []
-    for with_logits in (True, False):
-        m = evk_b200.Llm(2, 256, 4, 512, V, 3, 48, dtype=1, tied_embeddings=tied)
-        m.init_random(seed=21, std=0.05)
-        tok = torch.from_numpy(np.random.default_rng(4).integers(0, V, size=(3, 20)).astype(np.int32)).cuda()
-        nxt = torch.zeros(3, dtype=torch.int32, device="cuda")
-        stream = torch.cuda.Stream()
-        ids = []
-        with torch.cuda.stream(stream):
-            lg = torch.empty(3, V, dtype=torch.bfloat16, device="cuda") if with_logits else None
-            m.prefill(tok, nxt, lg, stream=stream)
-            ids.append(nxt.clone())
-            cur = nxt.clone()
-            for _ in range(5):
-                out = torch.zeros(3, dtype=torch.int32, device="cuda")
-                m.decode(cur, out, lg, stream=stream)
-                ids.append(out)
-                cur = out
-        torch.cuda.synchronize()
-        runs.append(torch.stack(ids).cpu().numpy())
-        m.close()
-    assert np.array_equal(runs[0], runs[1]), (runs[0], runs[1])
+    ref = RefModel(2, 256, 4, 512, V, tied, dtype=1, seed=21, std=0.05)
+    m = evk_b200.Llm(2, 256, 4, 512, V, 3, 48, dtype=1, tied_embeddings=tied)
+    load_weights(m, ref, torch.bfloat16)
+    prompt = np.random.default_rng(4).integers(0, V, size=(3, 20))
+    stats = teacher_forced_parity(ref, m, prompt, 5, 1, torch.bfloat16, 48, f"fused-head tied={tied}")
+    m.close()
+    assert stats["fused_ids_equal_oracle"] + len(stats["close_calls"]) == stats["checked"]
 
 
 @pytest.mark.parametrize("dtype", [0, 1])

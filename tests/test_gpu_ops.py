@@ -197,3 +197,26 @@ def test_greedy_sample(dtype, B, S, V, pos, base, count, ties):
         oracle.greedy_sample(l, ref, B, S, V, pos, base, count, dc)
         got = out.cpu().numpy().view(ndt)
         assert np.array_equal(got, ref), "greedy ids must be bit-exact"
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("V", [1000, 128256])
+def test_greedy_sample_signed_zero_max(dtype, V):
+    """A row whose maximum is 0, held by -0.0 in an earlier lane and +0.0 in a
+    later one: the reference's `>` treats the two zeros as equal, so its lane
+    tie rule (not the sign) decides the id."""
+    dc = dcode(dtype)
+    B = 2
+    vals = -1.0 - np.abs(np.random.default_rng(V).standard_normal(B * V)).astype(np.float32)
+    vals = vals.reshape(B, V)
+    vals[0, 3], vals[0, 7] = -0.0, 0.0        # lane 3 (bit-reversed 192) beats lane 7 (224)
+    vals[1, 700 % V], vals[1, 12] = 0.0, -0.0  # lane 12 vs lane 700 % 256
+    l = oracle.from_float(vals.ravel(), dc)
+    assert l.reshape(B, V)[0, 3] in (0x8000,), "quantiser must keep -0.0"
+    t = dev(l, dtype).view(B, 1, V)
+    out = torch.zeros(B, dtype=torch.int32, device="cuda")
+    ev().greedy_sample(t, out, 0, 0, V)
+    ref = np.zeros(B, np.uint32)
+    oracle.greedy_sample(l, ref, B, 1, V, 0, 0, V, dc)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), ref), (out, ref)
+    assert ref[0] == 3

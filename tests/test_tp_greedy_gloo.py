@@ -26,6 +26,8 @@ def bitrev8(x):
 def key(v, j):
     if not (v > -FMAX):
         return 0
+    if v == 0:
+        v = 0.0  # -0.0 ties with +0.0, as `>` treats them
     u = np.float32(v).view(np.uint32).item()
     u = (~u & 0xFFFFFFFF) if (u & 0x80000000) else (u | 0x80000000)
     rank = (bitrev8(j & 255) << 24) | (j >> 8)
@@ -62,10 +64,12 @@ def worker(rank, world, port, logits_f, out):
 @pytest.mark.parametrize("seed", [0, 1])
 def test_sharded_greedy_matches_reference_rule(seed):
     rng = np.random.default_rng(seed)
-    B, V = 3, 2048
+    B, V = 4, 2048
     vals = rng.integers(-3, 3, size=(B, V)).astype(np.float32)
     vals[0, 5] = vals[0, 5 + 1024] = 9.0  # tie across the two shards
     vals[1, 300] = vals[1, 44] = 9.0      # tie inside shard 0, different lanes
+    vals[3] = -1.0 - np.abs(vals[3])      # maximum 0 held by -0.0 (lane 3) and +0.0 (lane 7):
+    vals[3, 3], vals[3, 7 + 1024] = -0.0, 0.0  # the lower bit-reversed lane (3) wins
     logits = oracle.from_float(vals.ravel())
     logits_f = oracle.to_float(logits).reshape(B, V)
     ref = np.zeros(B, np.uint32)
