@@ -26,6 +26,7 @@ MM_TRANSPOSE_A = 1
 MM_TRANSPOSE_B = 2
 MM_ACC_C = 4
 ATTN_CAUSAL = 1
+ATTN_BWD_NORMALIZED = 2
 
 STATUS = {
     0: "OK",
@@ -70,6 +71,23 @@ SIGNATURES = {
     "evkcu_embed": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _int, _vp],
     "evkcu_greedy_sample": [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _int, _vp],
     "evkcu_greedy_sample_noalloc": [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _int, _vp],
+    # training side
+    "evkcu_relu": [_vp, _vp, _u64, _int, _vp],
+    "evkcu_relu_backward": [_vp, _vp, _vp, _u64, _int, _vp],
+    "evkcu_gelu_backward": [_vp, _vp, _vp, _u64, _int, _vp],
+    "evkcu_softmax_backward": [_vp, _vp, _vp, _u32, _u32, _f32, _int, _vp],
+    "evkcu_rms_norm_backward": [_vp, _vp, _vp, _u32, _u32, _f32, _int, _vp],
+    "evkcu_rope_backward": [_vp, _vp, _u32, _u32, _u32, _f32, _int, _vp],
+    "evkcu_embed_backward": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _int, _vp],
+    "evkcu_position_add": [_vp, _vp, _vp, _u32, _u32, _u32, _int, _vp],
+    "evkcu_position_add_backward": [_vp, _vp, _vp, _u32, _u32, _u32, _int, _vp],
+    "evkcu_sum_batch": [_vp, _vp, _u32, _u64, _int, _vp],
+    "evkcu_sgd": [_vp, _vp, _u64, _f32, _int, _vp],
+    "evkcu_adam": [_vp, _vp, _vp, _vp, _u64, _u32, _f32, _f32, _f32, _f32, _int, _vp],
+    "evkcu_mse_loss": [_vp, _vp, _vp, _vp, _u64, _int, _vp],
+    "evkcu_cross_entropy_loss": [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _int, _vp],
+    "evkcu_flash_attention_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _u32,
+                                  _int, _vp],
 }
 _RET = {
     "evkcu_last_error": ctypes.c_char_p,
@@ -281,6 +299,121 @@ def greedy_sample(logits, out, position, token_base, token_count, stream=None):
         _ptr(logits), _ptr(out), B, S, V, position, token_base, token_count, ob, _dtype_code(logits),
         _stream(stream)))
     return out
+
+
+# ------------------------------------------------------------ training side --
+def relu(x, out, stream=None):
+    _check("evkcu_relu", lib().evkcu_relu(_ptr(x), _ptr(out), x.numel(), _dtype_code(x), _stream(stream)))
+    return out
+
+
+def relu_backward(grad_out, x, grad_in, stream=None):
+    _check("evkcu_relu_backward", lib().evkcu_relu_backward(_ptr(grad_out), _ptr(x), _ptr(grad_in), x.numel(),
+                                                            _dtype_code(x), _stream(stream)))
+    return grad_in
+
+
+def gelu_backward(grad_out, x, grad_in, stream=None):
+    _check("evkcu_gelu_backward", lib().evkcu_gelu_backward(_ptr(grad_out), _ptr(x), _ptr(grad_in), x.numel(),
+                                                            _dtype_code(x), _stream(stream)))
+    return grad_in
+
+
+def softmax_backward(probs, grad_out, grad_in, scale=1.0, stream=None):
+    L = probs.shape[-1]
+    _check("evkcu_softmax_backward", lib().evkcu_softmax_backward(
+        _ptr(probs), _ptr(grad_out), _ptr(grad_in), probs.numel() // L, L, scale, _dtype_code(probs),
+        _stream(stream)))
+    return grad_in
+
+
+def rms_norm_backward(x, grad_out, grad_in, eps=1e-4, stream=None):
+    D = x.shape[-1]
+    _check("evkcu_rms_norm_backward", lib().evkcu_rms_norm_backward(
+        _ptr(x), _ptr(grad_out), _ptr(grad_in), x.numel() // D, D, eps, _dtype_code(x), _stream(stream)))
+    return grad_in
+
+
+def rope_backward(grad_out, grad_in, batch, seq_len, dim, base=10000.0, stream=None):
+    _check("evkcu_rope_backward", lib().evkcu_rope_backward(_ptr(grad_out), _ptr(grad_in), batch, seq_len, dim,
+                                                            base, _dtype_code(grad_out), _stream(stream)))
+    return grad_in
+
+
+def embed_backward(grad_out, idx, grad_E, stream=None):
+    ib = 2 if idx.element_size() == 2 else 4
+    _check("evkcu_embed_backward", lib().evkcu_embed_backward(
+        _ptr(grad_out), _ptr(idx), _ptr(grad_E), grad_E.shape[0], grad_E.shape[1], idx.numel(), ib,
+        _dtype_code(grad_E), _stream(stream)))
+    return grad_E
+
+
+def position_add(x, pos, out, batch, seq_len, dim, stream=None):
+    _check("evkcu_position_add", lib().evkcu_position_add(_ptr(x), _ptr(pos), _ptr(out), batch, seq_len, dim,
+                                                          _dtype_code(x), _stream(stream)))
+    return out
+
+
+def position_add_backward(grad_out, grad_in, grad_pos, batch, seq_len, dim, stream=None):
+    _check("evkcu_position_add_backward", lib().evkcu_position_add_backward(
+        _ptr(grad_out), _ptr(grad_in), _ptr(grad_pos), batch, seq_len, dim, _dtype_code(grad_out),
+        _stream(stream)))
+    return grad_in, grad_pos
+
+
+def sum_batch(x, out, batch, size, stream=None):
+    _check("evkcu_sum_batch", lib().evkcu_sum_batch(_ptr(x), _ptr(out), batch, size, _dtype_code(x),
+                                                    _stream(stream)))
+    return out
+
+
+def sgd(param, grad, lr, stream=None):
+    _check("evkcu_sgd", lib().evkcu_sgd(_ptr(param), _ptr(grad), param.numel(), lr, _dtype_code(param),
+                                        _stream(stream)))
+    return param
+
+
+def adam(param, grad, m, v, step, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-4, stream=None):
+    """m, v: the AdamState buffers (zero-initialised, same dtype/size as param);
+    step: the state's timestep after increment (1 on the first call)."""
+    _check("evkcu_adam", lib().evkcu_adam(_ptr(param), _ptr(grad), _ptr(m), _ptr(v), param.numel(), step, lr, beta1,
+                                          beta2, eps, _dtype_code(param), _stream(stream)))
+    return param
+
+
+def mse_loss(pred, target, grad, result, stream=None):
+    _check("evkcu_mse_loss", lib().evkcu_mse_loss(_ptr(pred), _ptr(target), _ptr(grad), _ptr(result), pred.numel(),
+                                                  _dtype_code(pred), _stream(stream)))
+    return result
+
+
+def cross_entropy_loss(logits, targets, grad, result, stream=None):
+    """logits (rows, V); targets (rows,) int16/uint16 (reference) or int32."""
+    V = logits.shape[-1]
+    tb = 2 if targets.element_size() == 2 else 4
+    _check("evkcu_cross_entropy_loss", lib().evkcu_cross_entropy_loss(
+        _ptr(logits), _ptr(targets), _ptr(grad), _ptr(result), logits.numel() // V, V, tb, _dtype_code(logits),
+        _stream(stream)))
+    return result
+
+
+def flash_attention_bwd(q, k, v, o, dO, dQ, dK, dV, heads: Optional[int] = None, causal=False, normalized=False,
+                        scale: float = 0.0, stream=None):
+    """Gradients of flash_attention (evk_ai.cpp:371-473).  Layouts as
+    flash_attention; without `heads` the reference's multi-query call."""
+    B, N, D = q.shape
+    if heads is None:
+        Dh = k.shape[-1]
+        H, Hkv = D // Dh, 1
+    else:
+        H = heads
+        Dh = D // H
+        Hkv = k.shape[-1] // Dh
+    flags = (ATTN_CAUSAL if causal else 0) | (ATTN_BWD_NORMALIZED if normalized else 0)
+    _check("evkcu_flash_attention_bwd", lib().evkcu_flash_attention_bwd(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dO), _ptr(dQ), _ptr(dK), _ptr(dV), B, N, H, Hkv, Dh, scale, flags,
+        _dtype_code(q), _stream(stream)))
+    return dQ, dK, dV
 
 
 # ------------------------------------------------------------- LLM driver --

@@ -1,7 +1,7 @@
 // evk_ai.cpp — evk::ai operators on the B200 backend: shape logic from
 // evk_ai_dispatch.h, kernels from libevkcu (include/evkcu.h).
-// Replaces evk_ai.cpp of the reference (pipeline creation :30-246 and the
-// per-op bind/push/dispatch/barrier recording :254-1067).
+// Replaces evk_ai.cpp of the reference (pipeline creation :30-246, AdamState
+// :193-216 and the per-op bind/push/dispatch/barrier recording :254-1094).
 #include "evk_ai.h"
 
 #include <cstdio>
@@ -40,6 +40,10 @@ static const evk_b200::Backend& backend() {
         current_stream,       fatal,          evkcu_matmul,  evkcu_flash_attention, evkcu_single_query_attention,
         evkcu_rms_norm,       evkcu_rope,     evkcu_gelu,    evkcu_softmax,         evkcu_add,
         evkcu_scale,          evkcu_zero,     evkcu_causal_mask, evkcu_embed,       evkcu_greedy_sample,
+        evkcu_relu,           evkcu_relu_backward,     evkcu_gelu_backward,  evkcu_softmax_backward,
+        evkcu_rms_norm_backward, evkcu_rope_backward,  evkcu_embed_backward, evkcu_position_add,
+        evkcu_position_add_backward, evkcu_sum_batch,  evkcu_sgd,            evkcu_adam,
+        evkcu_mse_loss,       evkcu_cross_entropy_loss, evkcu_flash_attention_bwd,
     };
     return be;
 }
@@ -68,5 +72,62 @@ void rope(Tensor& in, Tensor& out, uint32_t B, uint32_t S, uint32_t D, float bas
 void scale(Tensor& t, float s) { evk_b200::scale(backend(), t, s); }
 void zero(Tensor& t) { evk_b200::zero(backend(), t); }
 void rms_norm(Tensor& in, Tensor& out, float eps) { evk_b200::rms_norm(backend(), in, out, eps); }
+
+// ------------------------------------------------------------ training side --
+void AdamState::init(uint32_t num_elements) {
+    const uint64_t bytes = (uint64_t)num_elements * sizeof(float16_t);
+    m_buffer = evk::CreateBuffer({.size = bytes, .usage = evk::BufferUsage::Storage | evk::BufferUsage::TransferDst});
+    v_buffer = evk::CreateBuffer({.size = bytes, .usage = evk::BufferUsage::Storage | evk::BufferUsage::TransferDst});
+    GetCmd().fill(m_buffer, 0u, bytes);
+    GetCmd().fill(v_buffer, 0u, bytes);
+    SubmitCmd(true);
+    t = 0;
+}
+void AdamState::reset() {
+    m_buffer = {};
+    v_buffer = {};
+    t = 0;
+}
+
+void flash_attention_bwd(Tensor& q, Tensor& k, Tensor& v, Tensor& o, Tensor& dO, Tensor& dQ, Tensor& dK, Tensor& dV,
+                         uint32_t heads) {
+    evk_b200::flash_attention_bwd(backend(), q, k, v, o, dO, dQ, dK, dV, heads);
+}
+void mse_loss(Tensor& pred, Tensor& target, Tensor& grad, Tensor& result) {
+    evk_b200::mse_loss(backend(), pred, target, grad, result);
+}
+void sgd(Tensor& p, Tensor& g, float lr) { evk_b200::sgd(backend(), p, g, lr); }
+// evk_ai.cpp:525-566: lazily creates the state, then steps it.
+void adam(Tensor& p, Tensor& g, AdamState& state, float lr, float beta1, float beta2, float eps) {
+    if (!state.m_buffer) state.init(p.shape.count());
+    state.t += 1;
+    evk_b200::adam(backend(), p, g, reinterpret_cast<void*>(state.m_buffer.GetReference()),
+                   reinterpret_cast<void*>(state.v_buffer.GetReference()), state.t, lr, beta1, beta2, eps);
+}
+void softmax_backward(Tensor& probs, Tensor& go, Tensor& gi, float s) {
+    evk_b200::softmax_backward(backend(), probs, go, gi, s);
+}
+void relu(Tensor& in, Tensor& out) { evk_b200::relu(backend(), in, out); }
+void relu_backward(Tensor& go, Tensor& in, Tensor& gi) { evk_b200::relu_backward(backend(), go, in, gi); }
+void gelu_backward(Tensor& go, Tensor& in, Tensor& gi) { evk_b200::gelu_backward(backend(), go, in, gi); }
+void cross_entropy_loss(Tensor& logits, Tensor& targets, Tensor& grad, Tensor& result) {
+    evk_b200::cross_entropy_loss(backend(), logits, targets, grad, result);
+}
+void embed_backward(Tensor& go, Tensor& idx, Tensor& gE) { evk_b200::embed_backward(backend(), go, idx, gE); }
+void position_add(Tensor& in, Tensor& pos, Tensor& out, uint32_t B, uint32_t S, uint32_t D) {
+    evk_b200::position_add(backend(), in, pos, out, B, S, D);
+}
+void position_add_backward(Tensor& go, Tensor& gi, Tensor& gp, uint32_t B, uint32_t S, uint32_t D) {
+    evk_b200::position_add_backward(backend(), go, gi, gp, B, S, D);
+}
+void rope_backward(Tensor& go, Tensor& gi, uint32_t B, uint32_t S, uint32_t D, float base) {
+    evk_b200::rope_backward(backend(), go, gi, B, S, D, base);
+}
+void sum_batch(Tensor& in, Tensor& out, uint32_t batch, uint32_t size) {
+    evk_b200::sum_batch(backend(), in, out, batch, size);
+}
+void rms_norm_backward(Tensor& in, Tensor& go, Tensor& gi, float eps) {
+    evk_b200::rms_norm_backward(backend(), in, go, gi, eps);
+}
 
 }  // namespace evk::ai

@@ -1,14 +1,15 @@
-// evk_ai.h — the evk::ai inference operator API (carloshgsilva/evk
-// evk_ai.h:13-16, 18-472, 474-615, 617-1073) on the B200 backend.
+// evk_ai.h — the evk::ai operator API (carloshgsilva/evk evk_ai.h:13-16,
+// 18-472, 474-615, 617-1073) on the B200 backend.
 //
 // Same names, signatures, argument meaning and tensor layout as the
-// reference for the inference path: every Tensor is 2-byte storage of
-// shape.count() elements, row-major with the last dimension contiguous; token
-// ids are raw unsigned 16-bit integers stored in the element slots.  Ops are
-// enqueued on the stream of GetCmd() and run in order; SubmitCmd(wait)
-// records a submission and optionally waits for it.  The training-side
-// operators of the reference (losses, optimisers, backward passes) are not
-// part of this backend.  Additive extensions live in evk_ai_ext.h.
+// reference: every Tensor is 2-byte storage of shape.count() elements,
+// row-major with the last dimension contiguous; token ids are raw unsigned
+// 16-bit integers stored in the element slots.  Ops are enqueued on the
+// stream of GetCmd() and run in order; SubmitCmd(wait) records a submission
+// and optionally waits for it.  Inference operators, the training side
+// (backward passes, losses, SGD / Adam) and the autograd Graph are all
+// here.  Additive extensions (bf16, 32-bit ids, causal / grouped-query
+// attention, decode attention) live in evk_ai_ext.h.
 #pragma once
 
 #include <cassert>
@@ -18,6 +19,7 @@
 #include <cstring>
 #include <functional>
 #include <memory>
+#include <unordered_map>
 #include <vector>
 
 #include "evk.h"
@@ -216,8 +218,19 @@ struct Tensor {
     }
 };
 
-// fp16 operator set (evk_ai.h:489-615, inference subset).
+// fp16 operator set (evk_ai.h:474-615).
 namespace evk::ai {
+// Adam moments of one parameter tensor in 2-byte storage (evk_ai.h:476-487):
+// m_buffer holds m / rms(v), v_buffer holds log2(rms(v)) + 41 (0 = empty).
+struct AdamState {
+    evk::Buffer m_buffer;
+    evk::Buffer v_buffer;
+    uint32_t t = 0;  // steps taken
+
+    void init(uint32_t num_elements);
+    void reset();
+};
+
 void initialize();
 void shutdown();
 
@@ -241,63 +254,215 @@ void rope(Tensor& input, Tensor& out, uint32_t batch_size, uint32_t seq_len, uin
 void scale(Tensor& tensor, float scale_factor);
 void zero(Tensor& tensor);
 void rms_norm(Tensor& input, Tensor& output, float eps = 1e-4f);
+
+// Training side.  Backward passes accumulate into their gradient tensor;
+// losses and flash_attention_bwd overwrite their outputs.
+void flash_attention_bwd(Tensor& q, Tensor& k, Tensor& v, Tensor& o, Tensor& dO, Tensor& dQ, Tensor& dK, Tensor& dV,
+                         uint32_t heads = 0);
+void mse_loss(Tensor& predicted, Tensor& target, Tensor& predGrad, Tensor& result);
+void sgd(Tensor& param, Tensor& gradient, float learning_rate);
+void adam(Tensor& param, Tensor& gradient, AdamState& state, float learning_rate = 0.001f, float beta1 = 0.9f,
+          float beta2 = 0.999f, float epsilon = 1e-4f);
+void softmax_backward(Tensor& probs, Tensor& grad_out, Tensor& grad_in, float scale_factor = 1.0f);
+void relu(Tensor& in, Tensor& out);
+void relu_backward(Tensor& grad_out, Tensor& in, Tensor& grad_in);
+void gelu_backward(Tensor& grad_out, Tensor& in, Tensor& grad_in);
+// logits (rows, V), targets (rows) uint16 ids, 0 = ignored position.
+void cross_entropy_loss(Tensor& logits, Tensor& targets, Tensor& grad, Tensor& result);
+void embed_backward(Tensor& grad_out, Tensor& indices, Tensor& grad_embeddings);
+void position_add(Tensor& input, Tensor& pos_emb, Tensor& out, uint32_t batch_size, uint32_t seq_len,
+                  uint32_t embed_dim);
+void position_add_backward(Tensor& grad_out, Tensor& grad_input, Tensor& grad_pos, uint32_t batch_size,
+                           uint32_t seq_len, uint32_t embed_dim);
+void rope_backward(Tensor& grad_out, Tensor& grad_input, uint32_t batch_size, uint32_t seq_len, uint32_t embed_dim,
+                   float rotary_base = 10000.0f);
+void sum_batch(Tensor& input, Tensor& output, uint32_t batch_count, uint32_t size_per_batch);
+void rms_norm_backward(Tensor& input, Tensor& grad_out, Tensor& grad_input, float eps = 1e-4f);
 }  // namespace evk::ai
 
-// Forward-only computation graph (evk_ai.h:617-1073, inference subset): a
-// list of nodes whose forward closures call evk::ai ops in insertion order.
+// Autograd graph (evk_ai.h:617-1073).  Nodes are created in use order; eval
+// runs every forward closure in that order and, with backward, zeroes every
+// gradient first and then runs the backward closures in reverse order, so a
+// node's gradient is complete before its own backward closure reads it.
+// Parameters (tensor(shape, true)) are updated by step (SGD) or step_adam.
 struct Graph {
     std::vector<std::unique_ptr<Tensor>> nodes;
     std::vector<Tensor*> params;
+    std::unordered_map<Tensor*, evk::ai::AdamState> adam_states;
+    std::unique_ptr<Tensor> scratch;  // reused temporary (batched matmul weight gradients)
 
+    Tensor& get_scratch(const Shape& shape) {
+        if (scratch && scratch->shape.count() >= shape.count())
+            scratch->shape = shape;
+        else
+            scratch = std::make_unique<Tensor>(shape);
+        return *scratch;
+    }
     Tensor& tensor(Shape shape, bool param = false) {
         nodes.push_back(std::make_unique<Tensor>(shape));
         if (param) params.push_back(nodes.back().get());
         return *nodes.back();
     }
+    // Same elements, new shape: forward copies the buffer, backward copies the gradient back.
+    Tensor& view(Tensor& a, Shape new_shape) {
+        assert(a.shape.count() == new_shape.count() && "view requires same number of elements");
+        Tensor& out = tensor(new_shape);
+        const uint64_t bytes = (uint64_t)a.shape.count() * sizeof(float16_t);
+        out.forward_fn = [&a, &out, bytes]() { evk::ai::GetCmd().copy(a.buffer, out.buffer, bytes); };
+        out.backward_fn = [&a, &out, bytes]() { evk::ai::GetCmd().copy(out.grad().buffer, a.grad().buffer, bytes); };
+        return out;
+    }
+    // (M,K)(K,N), (B,M,K)(K,N), (M,K)(B,K,N), (B,M,K)(B,K,N).
     Tensor& matmul(Tensor& a, Tensor& b, uint8_t tile_m = 16, uint8_t tile_n = 16) {
         Shape out;
-        if (a.shape.rank() == 2 && b.shape.rank() == 2)
+        const uint32_t ra = a.shape.rank(), rb = b.shape.rank();
+        if (ra == 2 && rb == 2)
             out = Shape({a.shape[0], b.shape[1]});
-        else if (a.shape.rank() == 3 && b.shape.rank() == 2)
+        else if (ra == 3 && rb == 2)
             out = Shape({a.shape[0], a.shape[1], b.shape[1]});
-        else if (a.shape.rank() == 2 && b.shape.rank() == 3)
+        else if (ra == 2 && rb == 3)
             out = Shape({b.shape[0], a.shape[0], b.shape[2]});
-        else
+        else {
+            assert(ra == 3 && rb == 3 && "Unsupported matmul shapes");
             out = Shape({a.shape[0], a.shape[1], b.shape[2]});
+        }
         Tensor& c = tensor(out);
         c.forward_fn = [&a, &b, &c, tile_m, tile_n]() { evk::ai::matmul(a, b, c, false, false, false, tile_m, tile_n); };
+        c.backward_fn = [this, &a, &b, &c, tile_m, tile_n]() {
+            // dA += dC B^T
+            evk::ai::matmul(c.grad(), b, a.grad(), false, true, true, tile_m, tile_n);
+            if (a.shape.rank() == 3 && b.shape.rank() == 2) {
+                // dB += sum over the batch of A[i]^T dC[i]
+                const uint32_t nb = a.shape[0], K = a.shape[2], N = b.shape[1];
+                Tensor& per_batch = get_scratch(Shape({nb, K, N}));
+                evk::ai::matmul(a, c.grad(), per_batch, true, false, false, tile_m, tile_n);
+                evk::ai::sum_batch(per_batch, b.grad(), nb, K * N);
+            } else {
+                evk::ai::matmul(a, c.grad(), b.grad(), true, false, true, tile_m, tile_n);
+            }
+        };
         return c;
     }
     Tensor& add(Tensor& a, Tensor& b) {
         Tensor& c = tensor(a.shape);
         c.forward_fn = [&a, &b, &c]() { evk::ai::add(a, b, c); };
+        c.backward_fn = [&a, &b, &c]() {
+            evk::ai::add(a.grad(), c.grad(), a.grad());
+            evk::ai::add(b.grad(), c.grad(), b.grad());
+        };
         return c;
     }
     Tensor& residual(Tensor& a, Tensor& b) { return add(a, b); }
-    Tensor& gelu(Tensor& in) {
-        Tensor& out = tensor(in.shape);
-        out.forward_fn = [&in, &out]() { evk::ai::gelu(in, out); };
+    // The loss kernel writes predicted's gradient itself; there is no backward closure.
+    Tensor& mse_loss(Tensor& predicted, Tensor& target) {
+        assert(predicted.shape.rank() == target.shape.rank() && "mse_loss: predicted and target must have the same rank");
+        Tensor& loss = tensor(Shape({1}));
+        loss.forward_fn = [&predicted, &target, &loss]() { evk::ai::mse_loss(predicted, target, predicted.grad(), loss); };
+        return loss;
+    }
+    Tensor& relu(Tensor& a) {
+        Tensor& out = tensor(a.shape);
+        out.forward_fn = [&a, &out]() { evk::ai::relu(a, out); };
+        out.backward_fn = [&a, &out]() { evk::ai::relu_backward(out.grad(), a, a.grad()); };
         return out;
     }
-    Tensor& rms_norm(Tensor& in, float eps = 1e-4f) {
-        Tensor& out = tensor(in.shape);
-        out.forward_fn = [&in, &out, eps]() { evk::ai::rms_norm(in, out, eps); };
+    Tensor& gelu(Tensor& a) {
+        Tensor& out = tensor(a.shape);
+        out.forward_fn = [&a, &out]() { evk::ai::gelu(a, out); };
+        out.backward_fn = [&a, &out]() { evk::ai::gelu_backward(out.grad(), a, a.grad()); };
+        return out;
+    }
+    // out = a * factor; backward scales out's gradient in place (no later
+    // reader remains in reverse order) and adds it to a's.
+    Tensor& scale(Tensor& a, float factor) {
+        Tensor& out = tensor(a.shape);
+        const uint64_t bytes = (uint64_t)a.shape.count() * sizeof(float16_t);
+        out.forward_fn = [&a, &out, factor, bytes]() {
+            evk::ai::GetCmd().copy(a.buffer, out.buffer, bytes);
+            evk::ai::scale(out, factor);
+        };
+        out.backward_fn = [&a, &out, factor]() {
+            evk::ai::scale(out.grad(), factor);
+            evk::ai::add(a.grad(), out.grad(), a.grad());
+        };
+        return out;
+    }
+    Tensor& rms_norm(Tensor& input, float eps = 1e-4f) {
+        assert(input.shape.rank() >= 2 && "rms_norm expects at least 2D tensor");
+        Tensor& out = tensor(input.shape);
+        out.forward_fn = [&input, &out, eps]() { evk::ai::rms_norm(input, out, eps); };
+        out.backward_fn = [&input, &out, eps]() { evk::ai::rms_norm_backward(input, out.grad(), input.grad(), eps); };
+        return out;
+    }
+    // input (B, N, D) + pos_emb (N, D) broadcast over the batch.
+    Tensor& add_position_embedding(Tensor& input, Tensor& pos_emb, uint32_t batch_size, uint32_t seq_len) {
+        const uint32_t D = pos_emb.shape[1];
+        assert(input.shape.rank() == 3 && input.shape[0] == batch_size && input.shape[1] == seq_len &&
+               input.shape[2] == D && pos_emb.shape[0] == seq_len);
+        Tensor& out = tensor(input.shape);
+        out.forward_fn = [&input, &pos_emb, &out, batch_size, seq_len, D]() {
+            evk::ai::position_add(input, pos_emb, out, batch_size, seq_len, D);
+        };
+        out.backward_fn = [&input, &pos_emb, &out, batch_size, seq_len, D]() {
+            evk::ai::position_add_backward(out.grad(), input.grad(), pos_emb.grad(), batch_size, seq_len, D);
+        };
         return out;
     }
     Tensor& rope(Tensor& in, float base = 10000.0f) {
+        assert(in.shape.rank() == 3 && "rope expects (B, N, D)");
+        assert(in.shape[2] % 2u == 0u && "rope requires an even embedding dimension");
         Tensor& out = tensor(in.shape);
         const uint32_t B = in.shape[0], S = in.shape[1], D = in.shape[2];
         out.forward_fn = [&in, &out, B, S, D, base]() { evk::ai::rope(in, out, B, S, D, base); };
+        out.backward_fn = [&in, &out, B, S, D, base]() { evk::ai::rope_backward(out.grad(), in.grad(), B, S, D, base); };
         return out;
     }
+    // embeddings (V, D), indices (B, N) of uint16 ids -> (B, N, D).
     Tensor& embed(Tensor& embeddings, Tensor& indices) {
+        assert(indices.shape.rank() == 2 && "indices must be (B, N)");
         Tensor& out = tensor(Shape({indices.shape[0], indices.shape[1], embeddings.shape[1]}));
         out.forward_fn = [&embeddings, &indices, &out]() { evk::ai::embed(embeddings, indices, out); };
+        out.backward_fn = [&embeddings, &indices, &out]() {
+            evk::ai::embed_backward(out.grad(), indices, embeddings.grad());
+        };
         return out;
     }
-    // Unfused causal attention, one head over the whole model dimension
-    // (evk_ai.h:961-1007): scores = q k^T, mask, softmax(scale), probs v.
+    // logits (B, N, V), targets (B, N) uint16 ids (0 = ignored) -> mean loss.
+    // The forward computes the loss and the logits' gradient into a private
+    // (B*N, V) tensor; the backward recomputes it (logits may have changed
+    // since an earlier eval) and copies it to the logits' gradient.
+    Tensor& cross_entropy_loss(Tensor& logits, Tensor& targets) {
+        assert(logits.shape.rank() == 3 && "logits must be (B, N, V)");
+        assert(targets.shape.rank() == 2 && "targets must be (B, N)");
+        const uint32_t B = logits.shape[0], N = logits.shape[1], V = logits.shape[2];
+        Tensor& flat_grad = tensor(Shape({B * N, V}));
+        Tensor& loss = tensor(Shape({1}));
+        auto run = [&logits, &targets, &loss, &flat_grad, B, N, V]() {
+            Tensor flat_logits = Tensor::alias(Shape({B * N, V}), logits.buffer);
+            Tensor flat_targets = Tensor::alias(Shape({B * N}), targets.buffer);
+            evk::ai::cross_entropy_loss(flat_logits, flat_targets, flat_grad, loss);
+        };
+        loss.forward_fn = run;
+        loss.backward_fn = [run, &logits, &flat_grad]() {
+            run();
+            evk::ai::GetCmd().copy(flat_grad.buffer, logits.grad().buffer,
+                                   (uint64_t)logits.shape.count() * sizeof(float16_t));
+        };
+        return loss;
+    }
+    Tensor& softmax(Tensor& input, float input_scale = 1.0f) {
+        Tensor& out = tensor(input.shape);
+        out.forward_fn = [&input, &out, input_scale]() { evk::ai::softmax(input, out, input_scale); };
+        out.backward_fn = [&input, &out, input_scale]() {
+            evk::ai::softmax_backward(out, out.grad(), input.grad(), input_scale);
+        };
+        return out;
+    }
+    // Unfused causal attention, one head over the whole model dimension:
+    // scores = q k^T, mask, softmax(scale), probs v; scores and probs
+    // (B, N, N) are graph nodes.  scale <= 0 means 1/sqrt(D).
     Tensor& causal_attention(Tensor& q, Tensor& k, Tensor& v, float scale = 0.0f) {
+        assert(q.shape.rank() == 3 && k.shape.rank() == 3 && v.shape.rank() == 3);
         const uint32_t B = q.shape[0], N = q.shape[1], D = q.shape[2];
         Tensor& scores = tensor(Shape({B, N, N}));
         Tensor& probs = tensor(Shape({B, N, N}));
@@ -309,16 +474,37 @@ struct Graph {
             evk::ai::softmax(scores, probs, s);
             evk::ai::matmul(probs, v, out, false, false, false, 16, 16);
         };
+        out.backward_fn = [&q, &k, &v, &scores, &probs, &out, s]() {
+            evk::ai::matmul(out.grad(), v, probs.grad(), false, true, false, 16, 16);  // dP = dO v^T
+            evk::ai::matmul(probs, out.grad(), v.grad(), true, false, true, 16, 16);   // dv += P^T dO
+            evk::ai::softmax_backward(probs, probs.grad(), scores.grad(), s);
+            evk::ai::matmul(scores.grad(), k, q.grad(), false, false, true, 16, 16);   // dq += dS k
+            evk::ai::matmul(scores.grad(), q, k.grad(), true, false, true, 16, 16);    // dk += dS^T q
+        };
         return out;
     }
-    // Runs every forward closure in insertion order (evk_ai.h:1018-1048);
-    // backward passes are not part of this backend.
     void eval(bool backward = false, bool submit = true, bool wait = true) {
-        assert(!backward && "backward passes are not part of the inference backend");
-        (void)backward;
         evk::ai::GetCmd();
+        if (backward)
+            for (auto& n : nodes) evk::ai::zero(n->grad());
         for (auto& n : nodes)
             if (n->forward_fn) n->forward_fn();
+        if (backward)
+            for (size_t i = nodes.size(); i-- > 0;)
+                if (nodes[i]->backward_fn) nodes[i]->backward_fn();
         if (submit) evk::ai::SubmitCmd(wait);
+    }
+    void step(float lr = 0.001f) {
+        for (Tensor* p : params) {
+            assert(p->grad_tensor);
+            evk::ai::sgd(*p, p->grad(), lr);
+        }
+    }
+    void step_adam(float lr = 0.001f, float beta1 = 0.9f, float beta2 = 0.999f, float epsilon = 1e-4f) {
+        for (Tensor* p : params) evk::ai::adam(*p, p->grad(), adam_states[p], lr, beta1, beta2, epsilon);
+    }
+    void reset_adam() {
+        for (auto& kv : adam_states) kv.second.reset();
+        adam_states.clear();
     }
 };

@@ -37,6 +37,23 @@ struct Backend {
     int (*embed)(const void*, const void*, void*, uint32_t, uint32_t, uint32_t, uint32_t, int, void*);
     int (*greedy_sample)(const void*, void*, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, int,
                          void*);
+    // training side
+    int (*relu)(const void*, void*, uint64_t, int, void*);
+    int (*relu_backward)(const void*, const void*, void*, uint64_t, int, void*);
+    int (*gelu_backward)(const void*, const void*, void*, uint64_t, int, void*);
+    int (*softmax_backward)(const void*, const void*, void*, uint32_t, uint32_t, float, int, void*);
+    int (*rms_norm_backward)(const void*, const void*, void*, uint32_t, uint32_t, float, int, void*);
+    int (*rope_backward)(const void*, void*, uint32_t, uint32_t, uint32_t, float, int, void*);
+    int (*embed_backward)(const void*, const void*, void*, uint32_t, uint32_t, uint32_t, uint32_t, int, void*);
+    int (*position_add)(const void*, const void*, void*, uint32_t, uint32_t, uint32_t, int, void*);
+    int (*position_add_backward)(const void*, void*, void*, uint32_t, uint32_t, uint32_t, int, void*);
+    int (*sum_batch)(const void*, void*, uint32_t, uint64_t, int, void*);
+    int (*sgd)(void*, const void*, uint64_t, float, int, void*);
+    int (*adam)(void*, const void*, void*, void*, uint64_t, uint32_t, float, float, float, float, int, void*);
+    int (*mse_loss)(const void*, const void*, void*, void*, uint64_t, int, void*);
+    int (*cross_entropy_loss)(const void*, const void*, void*, void*, uint32_t, uint32_t, uint32_t, int, void*);
+    int (*flash_attention_bwd)(const void*, const void*, const void*, const void*, const void*, void*, void*, void*,
+                               uint32_t, uint32_t, uint32_t, uint32_t, uint32_t, float, uint32_t, int, void*);
 };
 
 template <class T>
@@ -175,6 +192,126 @@ void rms_norm(const Backend& be, T& in, T& out, float eps, const void* gamma = n
     if (!same_shape(in, out)) return be.fail(EVKCU_BAD_SHAPE, "rms_norm: shape mismatch");
     const uint32_t D = in.shape[-1];
     check(be, be.rms_norm(dptr(in), dmut(out), gamma, in.shape.count() / D, D, eps, dtype, be.stream()), "rms_norm");
+}
+
+// ------------------------------------------------------------ training side --
+// evk_ai.cpp:635-677, 700-720: elementwise over the input's element count.
+template <class T>
+void relu(const Backend& be, T& in, T& out, int dtype = EVKCU_F16) {
+    if (!same_shape(in, out)) return be.fail(EVKCU_BAD_SHAPE, "relu: shape mismatch");
+    check(be, be.relu(dptr(in), dmut(out), in.shape.count(), dtype, be.stream()), "relu");
+}
+template <class T>
+void relu_backward(const Backend& be, T& go, T& in, T& gi, int dtype = EVKCU_F16) {
+    if (go.shape.count() != in.shape.count() || gi.shape.count() != in.shape.count())
+        return be.fail(EVKCU_BAD_SHAPE, "relu_backward: size mismatch");
+    check(be, be.relu_backward(dptr(go), dptr(in), dmut(gi), in.shape.count(), dtype, be.stream()), "relu_backward");
+}
+template <class T>
+void gelu_backward(const Backend& be, T& go, T& in, T& gi, int dtype = EVKCU_F16) {
+    if (go.shape.count() != in.shape.count() || gi.shape.count() != in.shape.count())
+        return be.fail(EVKCU_BAD_SHAPE, "gelu_backward: size mismatch");
+    check(be, be.gelu_backward(dptr(go), dptr(in), dmut(gi), in.shape.count(), dtype, be.stream()), "gelu_backward");
+}
+// evk_ai.cpp:614-633: rows = count / last dim of probs.
+template <class T>
+void softmax_backward(const Backend& be, T& probs, T& go, T& gi, float scale, int dtype = EVKCU_F16) {
+    const uint32_t L = probs.shape[-1];
+    if (go.shape.count() != probs.shape.count() || gi.shape.count() != probs.shape.count())
+        return be.fail(EVKCU_BAD_SHAPE, "softmax_backward: size mismatch");
+    check(be, be.softmax_backward(dptr(probs), dptr(go), dmut(gi), probs.shape.count() / L, L, scale, dtype,
+                                  be.stream()),
+          "softmax_backward");
+}
+// evk_ai.cpp:1068-1092
+template <class T>
+void rms_norm_backward(const Backend& be, T& in, T& go, T& gi, float eps, int dtype = EVKCU_F16) {
+    const uint32_t D = in.shape[-1];
+    if (go.shape.count() != in.shape.count() || gi.shape.count() != in.shape.count())
+        return be.fail(EVKCU_BAD_SHAPE, "rms_norm_backward: size mismatch");
+    check(be, be.rms_norm_backward(dptr(in), dptr(go), dmut(gi), in.shape.count() / D, D, eps, dtype, be.stream()),
+          "rms_norm_backward");
+}
+// evk_ai.cpp:969-990
+template <class T>
+void rope_backward(const Backend& be, T& go, T& gi, uint32_t B, uint32_t S, uint32_t D, float base,
+                   int dtype = EVKCU_F16) {
+    if (D % 2 != 0) return be.fail(EVKCU_BAD_SHAPE, "rope_backward: odd embed_dim");
+    check(be, be.rope_backward(dptr(go), dmut(gi), B, S, D, base, dtype, be.stream()), "rope_backward");
+}
+// evk_ai.cpp:839-859: grad_E (V, D); indices any shape of uint16 ids.
+template <class T>
+void embed_backward(const Backend& be, T& go, T& idx, T& gE, uint32_t idx_bytes = 2, int dtype = EVKCU_F16) {
+    if (gE.shape.rank() != 2) return be.fail(EVKCU_BAD_SHAPE, "embed_backward: grad_embeddings must be rank 2");
+    const uint32_t V = gE.shape[0], D = gE.shape[1];
+    const uint32_t n = idx_bytes == 2 ? idx.shape.count() : idx.shape.count() / 2;
+    if (go.shape.count() != n * D) return be.fail(EVKCU_BAD_SHAPE, "embed_backward: grad_out size mismatch");
+    check(be, be.embed_backward(dptr(go), dptr(idx), dmut(gE), V, D, n, idx_bytes, dtype, be.stream()),
+          "embed_backward");
+}
+// evk_ai.cpp:883-944
+template <class T>
+void position_add(const Backend& be, T& in, T& pos, T& out, uint32_t B, uint32_t S, uint32_t D,
+                  int dtype = EVKCU_F16) {
+    check(be, be.position_add(dptr(in), dptr(pos), dmut(out), B, S, D, dtype, be.stream()), "position_add");
+}
+template <class T>
+void position_add_backward(const Backend& be, T& go, T& gi, T& gp, uint32_t B, uint32_t S, uint32_t D,
+                           int dtype = EVKCU_F16) {
+    check(be, be.position_add_backward(dptr(go), dmut(gi), dmut(gp), B, S, D, dtype, be.stream()),
+          "position_add_backward");
+}
+// evk_ai.cpp:1024-1043
+template <class T>
+void sum_batch(const Backend& be, T& in, T& out, uint32_t batch, uint32_t size, int dtype = EVKCU_F16) {
+    check(be, be.sum_batch(dptr(in), dmut(out), batch, size, dtype, be.stream()), "sum_batch");
+}
+// evk_ai.cpp:505-523
+template <class T>
+void sgd(const Backend& be, T& p, T& g, float lr, int dtype = EVKCU_F16) {
+    if (!same_shape(p, g)) return be.fail(EVKCU_BAD_SHAPE, "sgd: shape mismatch");
+    check(be, be.sgd(dmut(p), dptr(g), p.shape.count(), lr, dtype, be.stream()), "sgd");
+}
+// evk_ai.cpp:525-566: the caller owns the state and has incremented its step.
+template <class T>
+void adam(const Backend& be, T& p, T& g, void* m, void* v, uint32_t step, float lr, float b1, float b2, float eps,
+          int dtype = EVKCU_F16) {
+    if (!same_shape(p, g)) return be.fail(EVKCU_BAD_SHAPE, "adam: shape mismatch");
+    check(be, be.adam(dmut(p), dptr(g), m, v, p.shape.count(), step, lr, b1, b2, eps, dtype, be.stream()), "adam");
+}
+// evk_ai.cpp:481-503
+template <class T>
+void mse_loss(const Backend& be, T& pred, T& tgt, T& grad, T& result, int dtype = EVKCU_F16) {
+    if (!same_shape(pred, tgt) || result.shape.rank() != 1) return be.fail(EVKCU_BAD_SHAPE, "mse_loss: shapes");
+    check(be, be.mse_loss(dptr(pred), dptr(tgt), dmut(grad), dmut(result), pred.shape.count(), dtype, be.stream()),
+          "mse_loss");
+}
+// evk_ai.cpp:722-780: logits (rows, V), targets (rows) uint16 ids.
+template <class T>
+void cross_entropy_loss(const Backend& be, T& logits, T& tgt, T& grad, T& result, uint32_t target_bytes = 2,
+                        int dtype = EVKCU_F16) {
+    if (logits.shape.rank() != 2 || tgt.shape.rank() != 1 || result.shape.count() != 1)
+        return be.fail(EVKCU_BAD_SHAPE, "cross_entropy_loss: ranks");
+    const uint32_t rows = logits.shape[0], V = logits.shape[1];
+    if (tgt.shape[0] * 2 / target_bytes != rows || grad.shape.count() != logits.shape.count())
+        return be.fail(EVKCU_BAD_SHAPE, "cross_entropy_loss: shapes");
+    check(be, be.cross_entropy_loss(dptr(logits), dptr(tgt), dmut(grad), dmut(result), rows, V, target_bytes, dtype,
+                                    be.stream()),
+          "cross_entropy_loss");
+}
+// evk_ai.cpp:371-473: Q, O, dO, dQ (B, N, D = H*Dh); K, V, dK, dV (B, N, Dh).
+template <class T>
+void flash_attention_bwd(const Backend& be, T& q, T& k, T& v, T& o, T& dO, T& dQ, T& dK, T& dV, uint32_t heads,
+                         int dtype = EVKCU_F16) {
+    if (q.shape.rank() != 3 || k.shape.rank() != 3 || dQ.shape.rank() != 3 || dK.shape.rank() != 3)
+        return be.fail(EVKCU_BAD_SHAPE, "flash_attention_bwd: tensors must be rank 3");
+    const uint32_t B = q.shape[0], N = q.shape[1], D = q.shape[2], Dh = k.shape[2];
+    if (Dh == 0 || D % Dh != 0 || k.shape[0] != B || k.shape[1] != N || !same_shape(k, v) || !same_shape(q, dO) ||
+        !same_shape(q, dQ) || !same_shape(k, dK) || !same_shape(k, dV) || (heads != 0 && heads != D / Dh))
+        return be.fail(EVKCU_BAD_SHAPE, "flash_attention_bwd: incompatible shapes");
+    check(be, be.flash_attention_bwd(dptr(q), dptr(k), dptr(v), dptr(o), dptr(dO), dmut(dQ), dmut(dK), dmut(dV), B, N,
+                                     D / Dh, 1, Dh, 1.0f / std::sqrt((float)Dh), 0, dtype, be.stream()),
+          "flash_attention_bwd");
 }
 
 }  // namespace evk_b200

@@ -55,7 +55,7 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 // Scratch slots: each op family that needs global scratch owns one, so ops on
 // different streams never share scratch.  Scratch is zero-filled when it is
 // (re)allocated; kernels that use ticket counters leave them at zero.
-enum WorkspaceSlot { WS_GEMV = 0, WS_DECODE = 1, WS_GREEDY = 2, WS_COUNT = 3 };
+enum WorkspaceSlot { WS_GEMV = 0, WS_DECODE = 1, WS_GREEDY = 2, WS_TRAIN = 3, WS_COUNT = 4 };
 
 struct DeviceState {
     int device = -1;

@@ -29,38 +29,46 @@ namespace {
 using namespace sm100;
 
 constexpr int FM = 128;  // queries per tile (one TMEM lane per query)
-constexpr int FN = 128;  // keys per block
 constexpr uint32_t kTimeoutFlash = 0x201;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
 
 // NT query tiles per CTA, each with its own softmax warpgroup, share every
-// K/V block: while one tile's softmax runs, the tensor core works on the
-// other's S or PV.
-template <int DH, int NT>
+// K/V block of FN_ keys: while one tile's softmax runs, the tensor core works
+// on another's S or PV.  POLY_ of every 8 scores take their exponential from a
+// polynomial on the FMA pipe instead of the MUFU unit (ex2_poly2).
+//   Dh = 64:  four tiles over 64-key blocks: four softmax warps share each SM
+//             sub-partition, so one tile's exponentials overlap the others'
+//             row max, P store and barrier waits.
+//   Dh = 128: two tiles over 128-key blocks.
+template <int DH, int NT, int FN_, int POLY_ = 0>
 struct FlashCfg {
+    static constexpr int FN = FN_;    // keys per block
+    static constexpr int POLY = POLY_;
     static constexpr int Q_BYTES = FM * DH * 2;  // per tile
     static constexpr int KV_BYTES = FN * DH * 2;  // one K or V block
-    static constexpr int STAGES = NT == 2 ? (DH == 64 ? 5 : 2) : (DH == 64 ? 6 : 3);
-    // Dh = 128 with two tiles: S (128) + O (128) columns per tile fill TMEM,
-    // so P (16-bit pairs, 64 columns) is written over the tile's S, and
-    // S_t(j + 1) waits until PV_t(j) has read it.
-    static constexpr bool ALIAS_P = DH == 128 && NT == 2;
+    static constexpr int STAGES = NT == 4 ? 8 : NT == 2 ? (DH == 64 ? 5 : 2) : (DH == 64 ? 6 : 3);
+    static constexpr uint32_t TMEM_COLS = 512;
+    static constexpr int TSTRIDE = TMEM_COLS / NT;  // TMEM columns per tile
+    // Per tile t: S (fp32, FN columns), O (fp32, DH columns) and P (FN 16-bit
+    // values packed two per column, FN/2 columns).  When the three do not fit
+    // the tile's share of TMEM, P is written over the tile's S, and S_t(j + 1)
+    // waits until PV_t(j) has read it.
+    static constexpr bool ALIAS_P = FN + DH + FN / 2 > TSTRIDE;
+    static_assert(FN + DH <= TSTRIDE, "S and O must fit the tile's TMEM share");
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
     static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
     static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
-    static constexpr int SMEM = OFF_BAR + 256 + 1024;
+    static constexpr int BAR_BYTES = ((2 + 3 * STAGES + 5 * NT) * 8 + 16 + 127) / 128 * 128;
+    static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
     static constexpr int THREADS = 128 + NT * 128;
-    static constexpr uint32_t TMEM_COLS = 512;
-    // Per tile t: S (fp32, FN columns), O (fp32, DH columns) and P (FN 16-bit
-    // values packed two per column, FN/2 columns).
-    static __device__ __forceinline__ uint32_t col_s(int t) { return t * 256; }
-    static __device__ __forceinline__ uint32_t col_o(int t) { return t * 256 + FN; }
-    static __device__ __forceinline__ uint32_t col_p(int t) {
-        return ALIAS_P ? t * 256 : (NT == 2 ? t * 256 + FN + DH : FN + DH);
-    }
+    static __device__ __forceinline__ uint32_t col_s(int t) { return t * TSTRIDE; }
+    static __device__ __forceinline__ uint32_t col_o(int t) { return t * TSTRIDE + FN; }
+    static __device__ __forceinline__ uint32_t col_p(int t) { return ALIAS_P ? t * TSTRIDE : t * TSTRIDE + FN + DH; }
 };
-static_assert(FlashCfg<64, 2>::SMEM <= 227 * 1024 && FlashCfg<128, 2>::SMEM <= 227 * 1024, "flash smem");
+static_assert(FlashCfg<64, 2, 128>::SMEM <= 227 * 1024 && FlashCfg<128, 2, 128>::SMEM <= 227 * 1024 &&
+                  FlashCfg<64, 4, 64>::SMEM <= 227 * 1024,
+              "flash smem");
 
 // max(a, b, c) in one instruction (sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -92,6 +100,32 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
     return *reinterpret_cast<float2*>(&d);
 }
 
+// 2^x for a pair of x <= 0 on the FMA pipe (packed fp32x2), for the scores
+// whose exponential is not taken from MUFU.  Standard range reduction: with
+// x clamped to >= -126, t = x + 1.5 * 2^23 holds round(x) = j in its low
+// mantissa bits, f = x - j lies in [-1/2, 1/2], 2^f comes from a degree-3
+// polynomial, and j is added to the result's exponent field as an integer
+// (t's bits << 23 keep exactly j * 2^23 modulo 2^32).  The coefficients are a
+// minimax fit of 2^f on [-1/2, 1/2] in relative error (Lawson's iteratively
+// reweighted least squares, computed for this kernel): maximum relative error
+// 7.5e-5, below half a storage ulp of P in fp16 (2.4e-4).  -inf (a masked
+// score) gives about 2^-126, which rounds to 0 in P.
+__device__ __forceinline__ float2 ex2_poly2(float2 x) {
+    constexpr float kC0 = 0.9999280571937561f, kC1 = 0.6932609677314758f, kC2 = 0.24261116981506348f,
+                    kC3 = 0.0551716648042202f;
+    constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+    x.x = fmaxf(x.x, -126.0f);
+    x.y = fmaxf(x.y, -126.0f);
+    const float2 t = fadd2(x, make_float2(kShift, kShift));
+    const float2 j = fadd2(t, make_float2(-kShift, -kShift));
+    const float2 f = ffma2(j, make_float2(-1.0f, -1.0f), x);
+    float2 p = ffma2(f, make_float2(kC3, kC3), make_float2(kC2, kC2));
+    p = ffma2(p, f, make_float2(kC1, kC1));
+    p = ffma2(p, f, make_float2(kC0, kC0));
+    return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+}
+
 // Persistent kernel: one CTA per SM walks work items in zig-zag rounds
 // (see item_of); an item is NT consecutive 128-query tiles of
 // one (batch, head), heaviest causal items first.  Barriers, TMEM and the
@@ -116,14 +150,17 @@ __device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
 // Every barrier is waited on (or probed) for exactly one completion at a time,
 // and each barrier's next completion depends on the waiter having acted, so
 // parity waits are unambiguous across items.
-template <typename T, int DH, int NT>
-__global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
+template <typename T, typename Cfg, int DH, int NT>
+__global__ void __launch_bounds__(Cfg::THREADS, 1)
     flash_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, T* __restrict__ O, uint32_t N, uint32_t H,
                     uint32_t Hkv, uint32_t BH, float scale_log2, int causal, uint32_t idesc_s, uint32_t idesc_pv,
                     unsigned int* err) {
-    using Cfg = FlashCfg<DH, NT>;
     constexpr int ST = Cfg::STAGES;
+    constexpr int FN = Cfg::FN;
+    // Four tiles (P aliased over S): each P chunk goes to TMEM as soon as it
+    // is packed.  Two tiles: P is stored after the wait for PV_t(j - 1).
+    constexpr bool kEarlyP = Cfg::ALIAS_P && NT == 4;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sQ = smem + Cfg::OFF_Q;
@@ -158,7 +195,7 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
             q0[t] = (grp * NT + t) * FM;
-            nblk[t] = q0[t] < N ? (causal ? min(kv_all, q0[t] / FN + 1) : kv_all) : 0;
+            nblk[t] = q0[t] < N ? (causal ? min(kv_all, (q0[t] + FM + FN - 1) / FN) : kv_all) : 0;
         }
     };
 
@@ -198,7 +235,11 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *s_tmem;
-
+    // NT = 4: 640 threads leave 96 registers a thread at launch; the control
+    // warpgroup (producer, issuers) hands registers to the softmax
+    // warpgroups: 128 * 64 + 512 * 104 = 61,440 = 640 * 96.
+    if (warp < 4) {
+    if constexpr (NT == 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 64;\n" ::: "memory");
     if (warp == 0) {
         // ------------------------------------------------ TMA producer ----
         if (lane == 0) {
@@ -345,7 +386,9 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
                 if (nblk[t] > 0) ++ep[t];
             }
         }
-    } else if (warp >= 4) {
+    }
+    } else {
+        if constexpr (NT == 4) asm volatile("setmaxnreg.inc.sync.aligned.u32 104;\n" ::: "memory");
         // --------------------------------------------- softmax warps ----
         const int t = (warp >> 2) - 1;
         const int quarter = warp & 3;
@@ -383,7 +426,7 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
                 if (lane == 0) mbar_arrive(&s_free[t]);
 
                 const uint32_t k0 = j * FN;
-                const bool need_mask = (k0 + FN > N) || (causal && j + 1 == nb);
+                const bool need_mask = (k0 + FN > N) || (causal && k0 + FN > q0[t] + 1);
                 // Row max: three-input max, four independent accumulators.
                 float mxa[4];
 #pragma unroll
@@ -426,16 +469,31 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
                             // masked entries hold -inf: exp2(-inf) = 0
                             float2 x = ffma2(make_float2(__uint_as_float(sr[c][q * 8 + e]),
                                                          __uint_as_float(sr[c][q * 8 + e + 1])), sc2, nm2);
-                            f[e] = ex2(x.x);
-                            f[e + 1] = ex2(x.y);
+                            if (e < Cfg::POLY) {
+                                const float2 y = ex2_poly2(x);
+                                f[e] = y.x;
+                                f[e + 1] = y.y;
+                            } else {
+                                f[e] = ex2(x.x);
+                                f[e + 1] = ex2(x.y);
+                            }
                             rs2[e >> 1] = fadd2(rs2[e >> 1], make_float2(f[e], f[e + 1]));
                         }
                         const Vec8 pk = pack8<T>(f);
 #pragma unroll
                         for (int i = 0; i < 4; ++i) sr[c][q * 4 + i] = pk.w[i];
                     }
+                    if constexpr (kEarlyP) {
+                        // P over S: S_t(j) was issued only after PV_t(j - 1)
+                        // completed, so P_t(j - 1) has been read; storing each
+                        // chunk at once keeps fewer registers live.
+                        uint32_t pw[16];
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) pw[i] = sr[c][i];
+                        tmem_st16(p_addr + c * 16, pw);
+                    }
                 }
-                if (j > 0) {
+                if (!kEarlyP && j > 0) {
                     // PV_t(j-1) must be complete before the P columns are
                     // overwritten and before O is rescaled.
                     if (!mbar_wait(&pv_done[t], (gj - 1) & 1, s_abort, err, kTimeoutFlash)) {
@@ -448,22 +506,27 @@ __global__ void __launch_bounds__(FlashCfg<DH, NT>::THREADS, 1)
                                  ((rs2[2].x + rs2[2].y) + (rs2[3].x + rs2[3].y));
                 l = l * alpha + rs;
                 if (__any_sync(0xffffffffu, need)) {
+                    // (PV_t(j - 1) is complete: waited above, or implied by
+                    // S_t(j) when P is stored early over S.)
+                    constexpr int RC = kEarlyP ? 16 : 32;  // columns per TMEM round trip
 #pragma unroll
-                    for (int c = 0; c < DH / 32; ++c) {
-                        uint32_t rr[32];
-                        tmem_ld32(o_addr + c * 32, rr);
+                    for (int c = 0; c < DH / RC; ++c) {
+                        uint32_t rr[RC];
+                        if constexpr (RC == 16) tmem_ld16(o_addr + c * RC, rr); else tmem_ld32(o_addr + c * RC, rr);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
-                        tmem_st32(o_addr + c * 32, rr);
+                        for (int e = 0; e < RC; ++e) rr[e] = __float_as_uint(__uint_as_float(rr[e]) * alpha);
+                        if constexpr (RC == 16) tmem_st16(o_addr + c * RC, rr); else tmem_st32(o_addr + c * RC, rr);
                     }
                 }
+                if constexpr (!kEarlyP) {
 #pragma unroll
-                for (int c = 0; c < FN / 32; ++c) {
-                    uint32_t pw[16];
+                    for (int c = 0; c < FN / 32; ++c) {
+                        uint32_t pw[16];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) pw[i] = sr[c][i];
-                    tmem_st16(p_addr + c * 16, pw);
+                        for (int i = 0; i < 16; ++i) pw[i] = sr[c][i];
+                        tmem_st16(p_addr + c * 16, pw);
+                    }
                 }
                 // P and any O rescale (TMEM stores) must be complete before
                 // the PV MMA is issued.
@@ -562,10 +625,10 @@ __global__ void __launch_bounds__(256) flash_simt_kernel(const T* __restrict__ Q
     }
 }
 
-template <typename T, int DH, int NT>
+template <typename T, int DH, int NT, int FN, int POLY>
 int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N, uint32_t H,
                     uint32_t Hkv, float scale_log2, int causal, int dtype, uint64_t kv_bstride, cudaStream_t st) {
-    using Cfg = FlashCfg<DH, NT>;
+    using Cfg = FlashCfg<DH, NT, FN, POLY>;
     CUtensorMap mQ, mK, mV;
     int r;
     if ((r = make_tmap_3d(&mQ, q, (uint64_t)H * DH, N, B, (uint64_t)H * DH, (uint64_t)N * H * DH, 64, FM, dtype))) return r;
@@ -573,10 +636,19 @@ int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32
     // memory there (a KV cache): the map's row extent is N.
     if ((r = make_tmap_3d(&mK, k, (uint64_t)Hkv * DH, N, B, (uint64_t)Hkv * DH, kv_bstride, 64, FN, dtype))) return r;
     if ((r = make_tmap_3d(&mV, v, (uint64_t)Hkv * DH, N, B, (uint64_t)Hkv * DH, kv_bstride, 64, FN, dtype))) return r;
-    auto kern = flash_tc_kernel<T, DH, NT>;
+    auto kern = flash_tc_kernel<T, Cfg, DH, NT>;
     static bool attr = false;
     if (!attr) {
         EVKCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+        if (NT == 4) {
+            // The setmaxnreg split (64 registers for the control warpgroup,
+            // 104 for the four softmax warpgroups) must fit the registers the
+            // block is launched with, or the increase would wait forever.
+            cudaFuncAttributes fa{};
+            EVKCU_CUDA_TRY(cudaFuncGetAttributes(&fa, kern));
+            EVKCU_CHECK_ARG(fa.numRegs * Cfg::THREADS >= 128 * 64 + 512 * 104, EVKCU_CUDA_ERROR,
+                            "evkcu_flash_attention: kernel built with too few registers for its register split");
+        }
         attr = true;
     }
     const int bf = dtype == EVKCU_BF16 ? 1 : 0;
@@ -596,6 +668,20 @@ int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32
 using namespace evkcu;
 
 namespace evkcu {
+
+// Dh = 64 kernel variant, read once from EVKCU_FLASH64 (for A/B
+// measurement): 0 (default) two tiles over 128-key blocks, all exponentials
+// on MUFU; 1 four tiles over 64-key blocks, a quarter of the exponentials on
+// the FMA pipe; 2 four tiles, all on MUFU; 3 four tiles, half on the FMA pipe.
+// (Four tiles lose at C2: each S MMA reads the whole 128-row Q tile from
+// shared memory, which takes longer than its N = 64 columns of math.)
+static int flash64_variant() {
+    static const int v = [] {
+        const char* e = getenv("EVKCU_FLASH64");
+        return e ? atoi(e) : 0;
+    }();
+    return v;
+}
 
 int flash_attention_kv_strided(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N,
                                uint32_t H, uint32_t Hkv, uint32_t Dh, float scale, uint32_t flags, int dtype,
@@ -617,9 +703,24 @@ int flash_attention_kv_strided(const void* q, const void* k, const void* v, void
     const bool tma_ok = aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o) && kv_bstride % 8 == 0;
     if (tma_ok && (Dh == 64 || Dh == 128)) {
         return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
-            if (Dh == 64)
-                return launch_flash_tc<T, 64, 2>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, kv_bstride, st);
-            return launch_flash_tc<T, 128, 2>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, kv_bstride, st);
+            if (Dh == 64) {
+                switch (flash64_variant()) {
+                    case 1:
+                        return launch_flash_tc<T, 64, 4, 64, 2>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype,
+                                                                kv_bstride, st);
+                    case 2:
+                        return launch_flash_tc<T, 64, 4, 64, 0>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype,
+                                                                kv_bstride, st);
+                    case 3:
+                        return launch_flash_tc<T, 64, 4, 64, 4>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype,
+                                                                kv_bstride, st);
+                    default:
+                        return launch_flash_tc<T, 64, 2, 128, 0>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype,
+                                                                 kv_bstride, st);
+                }
+            }
+            return launch_flash_tc<T, 128, 2, 128, 0>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, kv_bstride,
+                                                      st);
         });
     }
     const uint64_t warps = (uint64_t)B * H * N;

@@ -50,6 +50,9 @@ typedef enum evkcu_dtype {
 
 /* flash attention flags (extension: the reference is non-causal only) */
 #define EVKCU_ATTN_CAUSAL 1u
+/* flash_attention_bwd only: use the exact softmax gradient term
+ * sum_j p_ij dp_ij (= t_i / l_i) instead of the reference shader's t_i.     */
+#define EVKCU_ATTN_BWD_NORMALIZED 2u
 
 /* ---- context -------------------------------------------------------------
  * Replaces evk::ai::initialize / shutdown (evk_ai.h:489-490, evk_ai.cpp:211-252):
@@ -189,6 +192,85 @@ int evkcu_single_query_attention_devlen(const void* q, const void* kcache, const
                                         uint32_t B, uint32_t H, uint32_t Hkv, uint32_t Dh,
                                         uint32_t max_len, const uint32_t* d_cur_len, float scale,
                                         int dtype, void* stream);
+
+/* ---- training side ---------------------------------------------------------
+ * The reference's training operators (evk_ai.h:474-615).  Backward passes
+ * accumulate into their gradient tensor (grad_in += ...) as the shaders do;
+ * losses and flash_attention_bwd overwrite their outputs.                    */
+
+/* evk::ai::relu / relu_backward, evk_ai.cpp:635-677, shaders/relu.comp,
+ * relu_bwd.comp: out = max(0, in); grad_in += in > 0 ? grad_out : 0.        */
+int evkcu_relu(const void* in, void* out, uint64_t n, int dtype, void* stream);
+int evkcu_relu_backward(const void* grad_out, const void* in, void* grad_in, uint64_t n, int dtype, void* stream);
+
+/* evk::ai::gelu_backward, evk_ai.cpp:702-720, shaders/gelu_bwd.comp:
+ * grad_in += grad_out * d gelu(in) / d in (tanh form).                      */
+int evkcu_gelu_backward(const void* grad_out, const void* in, void* grad_in, uint64_t n, int dtype, void* stream);
+
+/* evk::ai::softmax_backward, evk_ai.cpp:614-633, shaders/softmax_bwd.comp:
+ * per row grad_in += probs * (grad_out - dot(grad_out, probs)) * scale.    */
+int evkcu_softmax_backward(const void* probs, const void* grad_out, void* grad_in, uint32_t rows, uint32_t L,
+                           float scale, int dtype, void* stream);
+
+/* evk::ai::rms_norm_backward, evk_ai.cpp:1068-1092, shaders/rms_norm_bwd.comp:
+ * grad_in += (g - y dot(g, y) / D) / rms over rows of D.                    */
+int evkcu_rms_norm_backward(const void* in, const void* grad_out, void* grad_in, uint32_t rows, uint32_t D,
+                            float eps, int dtype, void* stream);
+
+/* evk::ai::rope_backward, evk_ai.cpp:969-990, shaders/rope_bwd.comp: the
+ * inverse rotation of rope over the whole last dimension, accumulated.      */
+int evkcu_rope_backward(const void* grad_out, void* grad_in, uint32_t batch, uint32_t seq_len, uint32_t dim,
+                        float base, int dtype, void* stream);
+
+/* evk::ai::embed_backward, evk_ai.cpp:839-859, shaders/embed_bwd.comp:
+ * grad_E[idx[i], :] += grad_out[i, :], indices in order, rounded per add.
+ * idx_bytes: 2 (reference) or 4 (extension).                                */
+int evkcu_embed_backward(const void* grad_out, const void* idx, void* grad_E, uint32_t vocab, uint32_t dim,
+                         uint32_t n_idx, uint32_t idx_bytes, int dtype, void* stream);
+
+/* evk::ai::position_add / position_add_backward, evk_ai.cpp:883-944,
+ * shaders/position_add.comp, position_add_bwd.comp: out = in + pos
+ * (broadcast over batch); grad_in += grad_out, grad_pos += sum_b grad_out.  */
+int evkcu_position_add(const void* in, const void* pos, void* out, uint32_t batch, uint32_t seq_len, uint32_t dim,
+                       int dtype, void* stream);
+int evkcu_position_add_backward(const void* grad_out, void* grad_in, void* grad_pos, uint32_t batch,
+                                uint32_t seq_len, uint32_t dim, int dtype, void* stream);
+
+/* evk::ai::sum_batch, evk_ai.cpp:1024-1043, shaders/sum_batch.comp:
+ * out[i] += sum_b in[b * size + i].                                          */
+int evkcu_sum_batch(const void* in, void* out, uint32_t batch, uint64_t size, int dtype, void* stream);
+
+/* evk::ai::sgd, evk_ai.cpp:505-523, shaders/sgd.comp: param -= lr * grad.   */
+int evkcu_sgd(void* param, const void* grad, uint64_t n, float lr, int dtype, void* stream);
+
+/* evk::ai::adam, evk_ai.cpp:525-566, shaders/adam.comp.  m and v are the
+ * AdamState buffers (2-byte storage: m normalised by rms, v as biased log2
+ * rms; zero-initialised); step is the state's timestep after increment
+ * (1 on the first call).                                                    */
+int evkcu_adam(void* param, const void* grad, void* m, void* v, uint64_t n, uint32_t step, float lr, float beta1,
+               float beta2, float eps, int dtype, void* stream);
+
+/* evk::ai::mse_loss, evk_ai.cpp:481-503, shaders/mse_loss.comp:
+ * grad = 2 (pred - target) / n, result[0] = mean((pred - target)^2).        */
+int evkcu_mse_loss(const void* pred, const void* target, void* grad, void* result, uint64_t n, int dtype,
+                   void* stream);
+
+/* evk::ai::cross_entropy_loss, evk_ai.cpp:722-780, shaders/cross_entropy*.comp:
+ * logits [rows, V], targets [rows] (target 0 = ignore); grad = (softmax -
+ * onehot) / valid_count on valid rows, 0 elsewhere; result[0] = mean loss
+ * over valid rows.  target_bytes: 2 (reference) or 4 (extension).           */
+int evkcu_cross_entropy_loss(const void* logits, const void* targets, void* grad, void* result, uint32_t rows,
+                             uint32_t V, uint32_t target_bytes, int dtype, void* stream);
+
+/* evk::ai::flash_attention_bwd, evk_ai.cpp:371-473,
+ * shaders/flash_attention_bwd.comp: gradients of O = softmax(Q K^T scale) V
+ * for Q, dO, dQ [B, N, H*Dh] and K, V, dK, dV [B, N, Hkv*Dh] (the reference
+ * is Hkv = 1, non-causal; flags may add EVKCU_ATTN_CAUSAL and
+ * EVKCU_ATTN_BWD_NORMALIZED).  scale <= 0 means 1/sqrt(Dh).  O is accepted
+ * for the reference's signature but not read (the forward is recomputed).  */
+int evkcu_flash_attention_bwd(const void* q, const void* k, const void* v, const void* o, const void* dO, void* dQ,
+                              void* dK, void* dV, uint32_t B, uint32_t N, uint32_t H, uint32_t Hkv, uint32_t Dh,
+                              float scale, uint32_t flags, int dtype, void* stream);
 
 /* ---- LLM driver (extension) ------------------------------------------------
  * The decoder that example/main_llm.cpp builds from these operators

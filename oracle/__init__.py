@@ -40,6 +40,21 @@ _SIGS = {
     "oracle_quantize": [_vp, _vp, _u64, _int],
     "oracle_dequantize": [_vp, _vp, _u64, _int],
     "oracle_num_threads": [],
+    "oracle_relu": [_vp, _vp, _u64, _int],
+    "oracle_relu_backward": [_vp, _vp, _vp, _u64, _int],
+    "oracle_gelu_backward": [_vp, _vp, _vp, _u64, _int],
+    "oracle_softmax_backward": [_vp, _vp, _vp, _u32, _u32, _f32, _int],
+    "oracle_rms_norm_backward": [_vp, _vp, _vp, _u32, _u32, _f32, _int],
+    "oracle_rope_backward": [_vp, _vp, _u32, _u32, _u32, _f32, _int],
+    "oracle_embed_backward": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _int],
+    "oracle_position_add": [_vp, _vp, _vp, _u32, _u32, _u32, _int],
+    "oracle_position_add_backward": [_vp, _vp, _vp, _u32, _u32, _u32, _int],
+    "oracle_sum_batch": [_vp, _vp, _u32, _u64, _int],
+    "oracle_sgd": [_vp, _vp, _u64, _f32, _int],
+    "oracle_adam": [_vp, _vp, _vp, _vp, _u64, _u32, _f32, _f32, _f32, _f32, _int],
+    "oracle_mse_loss": [_vp, _vp, _vp, _vp, _u64, _int],
+    "oracle_cross_entropy_loss": [_vp, _vp, _vp, _vp, _u32, _u32, _u32, _int],
+    "oracle_flash_attention_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _u32, _int],
 }
 
 _lib = None
@@ -154,3 +169,80 @@ def greedy_sample(logits, out, B, S, V, position, token_base, token_count, dtype
     lib().oracle_greedy_sample(_p(logits), _p(out), B, S, V, position, token_base, token_count, out.dtype.itemsize,
                                dtype)
     return out
+
+
+# ------------------------------------------------------------ training side --
+def relu(x, out, dtype=0):
+    lib().oracle_relu(_p(x), _p(out), x.size, dtype)
+    return out
+
+
+def relu_backward(go, x, gi, dtype=0):
+    lib().oracle_relu_backward(_p(go), _p(x), _p(gi), x.size, dtype)
+    return gi
+
+
+def gelu_backward(go, x, gi, dtype=0):
+    lib().oracle_gelu_backward(_p(go), _p(x), _p(gi), x.size, dtype)
+    return gi
+
+
+def softmax_backward(p, g, gi, rows, L, scale=1.0, dtype=0):
+    lib().oracle_softmax_backward(_p(p), _p(g), _p(gi), rows, L, scale, dtype)
+    return gi
+
+
+def rms_norm_backward(x, g, gi, rows, D, eps, dtype=0):
+    lib().oracle_rms_norm_backward(_p(x), _p(g), _p(gi), rows, D, eps, dtype)
+    return gi
+
+
+def rope_backward(go, gi, batch, seq, dim, base=10000.0, dtype=0):
+    lib().oracle_rope_backward(_p(go), _p(gi), batch, seq, dim, base, dtype)
+    return gi
+
+
+def embed_backward(go, idx, gE, vocab, dim, dtype=0):
+    lib().oracle_embed_backward(_p(go), _p(idx), _p(gE), vocab, dim, idx.size, idx.dtype.itemsize, dtype)
+    return gE
+
+
+def position_add(x, pos, out, batch, seq, dim, dtype=0):
+    lib().oracle_position_add(_p(x), _p(pos), _p(out), batch, seq, dim, dtype)
+    return out
+
+
+def position_add_backward(go, gi, gp, batch, seq, dim, dtype=0):
+    lib().oracle_position_add_backward(_p(go), _p(gi), _p(gp), batch, seq, dim, dtype)
+    return gi, gp
+
+
+def sum_batch(x, out, batch, size, dtype=0):
+    lib().oracle_sum_batch(_p(x), _p(out), batch, size, dtype)
+    return out
+
+
+def sgd(p, g, lr, dtype=0):
+    lib().oracle_sgd(_p(p), _p(g), p.size, lr, dtype)
+    return p
+
+
+def adam(p, g, m, v, step, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-4, dtype=0):
+    lib().oracle_adam(_p(p), _p(g), _p(m), _p(v), p.size, step, lr, beta1, beta2, eps, dtype)
+    return p
+
+
+def mse_loss(pred, tgt, grad, result, dtype=0):
+    lib().oracle_mse_loss(_p(pred), _p(tgt), _p(grad), _p(result), pred.size, dtype)
+    return result
+
+
+def cross_entropy_loss(logits, tgt, grad, result, rows, V, dtype=0):
+    lib().oracle_cross_entropy_loss(_p(logits), _p(tgt), _p(grad), _p(result), rows, V, tgt.dtype.itemsize, dtype)
+    return result
+
+
+def flash_attention_bwd(q, k, v, dO, dQ, dK, dV, B, N, H, Hkv, Dh, scale=0.0, flags=0, dtype=0):
+    lib().oracle_flash_attention_bwd(_p(q), _p(k), _p(v), _p(dO), _p(dQ), _p(dK), _p(dV), B, N, H, Hkv, Dh, scale,
+                                     flags, dtype)
+    return dQ, dK, dV

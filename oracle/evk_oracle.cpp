@@ -412,6 +412,257 @@ void oracle_greedy_sample(const uint16_t* logits, void* out, uint32_t B, uint32_
     }
 }
 
+// ---- training side -------------------------------------------------------
+// shaders/relu.comp: out = max(0, x)
+void oracle_relu(const uint16_t* in, uint16_t* out, uint64_t n, int dt) {
+    par_for((int64_t)n, [&](int64_t i) { out[i] = st(std::max(0.0f, ld(in, i, dt)), dt); }, 4096);
+}
+// shaders/relu_bwd.comp: gi += x > 0 ? go : 0
+void oracle_relu_backward(const uint16_t* go, const uint16_t* in, uint16_t* gi, uint64_t n, int dt) {
+    par_for((int64_t)n, [&](int64_t i) {
+        gi[i] = st(ld(gi, i, dt) + (ld(in, i, dt) > 0.0f ? ld(go, i, dt) : 0.0f), dt);
+    }, 4096);
+}
+// shaders/gelu_bwd.comp:16-37: gi += go * gelu'(x), tanh form
+void oracle_gelu_backward(const uint16_t* go, const uint16_t* in, uint16_t* gi, uint64_t n, int dt) {
+    par_for((int64_t)n, [&](int64_t i) {
+        const double x = ld(in, i, dt);
+        const double kA = 0.7978845608028654, kB = 0.044715;
+        const double t = std::tanh(kA * (x + kB * x * x * x));
+        const double g = 0.5 * (1.0 + t) + 0.5 * x * (1.0 - t * t) * kA * (1.0 + 3.0 * kB * x * x);
+        gi[i] = st((float)(ld(gi, i, dt) + ld(go, i, dt) * g), dt);
+    }, 4096);
+}
+// shaders/softmax_bwd.comp: gi += p (g - dot(g, p)) scale per row
+void oracle_softmax_backward(const uint16_t* p, const uint16_t* g, uint16_t* gi, uint32_t rows, uint32_t L,
+                             float scale, int dt) {
+    par_for((int64_t)rows, [&](int64_t r) {
+        const uint64_t b = (uint64_t)r * L;
+        double dot = 0.0;
+        for (uint32_t j = 0; j < L; ++j) dot += (double)ld(p, b + j, dt) * ld(g, b + j, dt);
+        for (uint32_t j = 0; j < L; ++j)
+            gi[b + j] = st((float)(ld(gi, b + j, dt) + ld(p, b + j, dt) * (ld(g, b + j, dt) - dot) * scale), dt);
+    });
+}
+// shaders/rms_norm_bwd.comp:21-74: x clamped to +-65504, rms = sqrt(mean x^2 + eps),
+// gi += g / rms - x / rms^2 * dot(g, x / rms) / D
+void oracle_rms_norm_backward(const uint16_t* x, const uint16_t* g, uint16_t* gi, uint32_t rows, uint32_t D,
+                              float eps, int dt) {
+    par_for((int64_t)rows, [&](int64_t r) {
+        const uint64_t b = (uint64_t)r * D;
+        auto xv = [&](uint32_t j) { return (double)std::min(std::max(ld(x, b + j, dt), -65504.0f), 65504.0f); };
+        double ss = 0.0;
+        for (uint32_t j = 0; j < D; ++j) ss += xv(j) * xv(j);
+        const double inv = 1.0 / std::sqrt(ss / D + (double)eps);
+        double dot = 0.0;
+        for (uint32_t j = 0; j < D; ++j) dot += ld(g, b + j, dt) * xv(j) * inv;
+        const double sc = dot / D;
+        for (uint32_t j = 0; j < D; ++j)
+            gi[b + j] = st((float)(ld(gi, b + j, dt) + ld(g, b + j, dt) * inv - xv(j) * inv * inv * sc), dt);
+    });
+}
+// shaders/rope_bwd.comp: transpose rotation (angle t * base^(-2p/D)), accumulated
+void oracle_rope_backward(const uint16_t* go, uint16_t* gi, uint32_t batch, uint32_t seq_len, uint32_t dim,
+                          float base, int dt) {
+    const uint64_t rows = (uint64_t)batch * seq_len;
+    par_for((int64_t)rows, [&](int64_t r) {
+        const float t = (float)(uint32_t)(r % seq_len);
+        for (uint32_t c = 0; c < dim; c += 2) {
+            const float inv_freq = std::pow(base, -2.0f * (float)(c / 2) / (float)dim);
+            const float ang = t * inv_freq;
+            const float cs = std::cos(ang), sn = std::sin(ang);
+            const uint64_t i0 = r * dim + c;
+            const float g0 = ld(go, i0, dt), g1 = ld(go, i0 + 1, dt);
+            gi[i0] = st(ld(gi, i0, dt) + g0 * cs + g1 * sn, dt);
+            gi[i0 + 1] = st(ld(gi, i0 + 1, dt) - g0 * sn + g1 * cs, dt);
+        }
+    }, 64);
+}
+// shaders/embed_bwd.comp: gE[idx[i], d] += go[i, d] over i in order, rounding after each add
+void oracle_embed_backward(const uint16_t* go, const void* idx, uint16_t* gE, uint32_t vocab, uint32_t dim,
+                           uint32_t n_idx, uint32_t idx_bytes, int dt) {
+    par_for((int64_t)dim, [&](int64_t d) {
+        for (uint32_t i = 0; i < n_idx; ++i) {
+            const uint32_t tok = idx_bytes == 2 ? ((const uint16_t*)idx)[i] : ((const uint32_t*)idx)[i];
+            if (tok >= vocab) continue;
+            const uint64_t o = (uint64_t)tok * dim + d;
+            gE[o] = st(ld(gE, o, dt) + ld(go, (uint64_t)i * dim + d, dt), dt);
+        }
+    });
+}
+// shaders/position_add.comp: out[b,t,d] = in[b,t,d] + pos[t,d]
+void oracle_position_add(const uint16_t* in, const uint16_t* pos, uint16_t* out, uint32_t batch, uint32_t seq_len,
+                         uint32_t dim, int dt) {
+    const uint64_t n = (uint64_t)batch * seq_len * dim, per = (uint64_t)seq_len * dim;
+    par_for((int64_t)n, [&](int64_t i) { out[i] = st(ld(in, i, dt) + ld(pos, i % per, dt), dt); }, 4096);
+}
+// shaders/sum_batch.comp: out[i] += sum_b in[b * size + i] (fp32, rounded once)
+void oracle_sum_batch(const uint16_t* in, uint16_t* out, uint32_t batch, uint64_t size, int dt) {
+    par_for((int64_t)size, [&](int64_t i) {
+        float s = ld(out, i, dt);
+        for (uint32_t b = 0; b < batch; ++b) s += ld(in, (uint64_t)b * size + i, dt);
+        out[i] = st(s, dt);
+    }, 4096);
+}
+// shaders/position_add_bwd.comp: mode 0 gi += go; mode 1 gp += sum_b go
+void oracle_position_add_backward(const uint16_t* go, uint16_t* gi, uint16_t* gp, uint32_t batch, uint32_t seq_len,
+                                  uint32_t dim, int dt) {
+    const uint64_t n = (uint64_t)batch * seq_len * dim;
+    par_for((int64_t)n, [&](int64_t i) { gi[i] = st(ld(gi, i, dt) + ld(go, i, dt), dt); }, 4096);
+    oracle_sum_batch(go, gp, batch, (uint64_t)seq_len * dim, dt);
+}
+// shaders/sgd.comp
+void oracle_sgd(uint16_t* p, const uint16_t* g, uint64_t n, float lr, int dt) {
+    par_for((int64_t)n, [&](int64_t i) { p[i] = st(ld(p, i, dt) - lr * ld(g, i, dt), dt); }, 4096);
+}
+// shaders/adam.comp with evk_ai.cpp:525-566 (bias corrections from the step)
+void oracle_adam(uint16_t* p, const uint16_t* g, uint16_t* mb, uint16_t* vb, uint64_t n, uint32_t step, float lr,
+                 float b1, float b2, float eps, int dt) {
+    const float c1 = 1.0f / (1.0f - std::pow(b1, (float)step));
+    const float c2 = 1.0f / (1.0f - std::pow(b2, (float)step));
+    par_for((int64_t)n, [&](int64_t i) {
+        const float grad = ld(g, i, dt);
+        if (std::isnan(grad) || std::isinf(grad)) return;
+        const float stored = ld(vb, i, dt);
+        float rms = stored > 0.0f ? std::exp2(stored - 41.0f) : 0.0f;
+        float m = ld(mb, i, dt) * rms;
+        float v = rms * rms;
+        m = b1 * m + (1.0f - b1) * grad;
+        v = b2 * v + (1.0f - b2) * grad * grad;
+        rms = std::sqrt(std::max(v, 0.0f));
+        const float mn = m / std::max(rms, 1.0e-8f);
+        if (!std::isnan(mn) && !std::isinf(mn)) mb[i] = st(mn, dt);
+        const float lg = std::log2(std::max(rms, 1.0e-12f)) + 41.0f;
+        if (!std::isnan(lg) && !std::isinf(lg)) vb[i] = st(lg, dt);
+        const float upd = lr * (m * c1) / (rms * std::sqrt(c2) + eps);
+        if (!std::isnan(upd) && !std::isinf(upd))
+            p[i] = st(std::min(std::max(ld(p, i, dt) - upd, -65504.0f), 65504.0f), dt);
+    }, 4096);
+}
+// shaders/mse_loss.comp: grad = 2 (p - t) / n; result = mean (p - t)^2
+void oracle_mse_loss(const uint16_t* pred, const uint16_t* tgt, uint16_t* grad, uint16_t* result, uint64_t n,
+                     int dt) {
+    double s = 0.0;
+    for (uint64_t i = 0; i < n; ++i) {
+        const float d = ld(pred, i, dt) - ld(tgt, i, dt);
+        s += (double)d * d;
+        grad[i] = st(2.0f / (float)n * d, dt);
+    }
+    result[0] = st((float)(s / (double)n), dt);
+}
+// shaders/cross_entropy_count.comp, cross_entropy.comp, cross_entropy_scale.comp:
+// logits clamped to +-65000; valid rows (0 < t < V) get
+// grad = (softmax - onehot(t)) / count and loss (max + ln sum e^(l - max) - l_t) / count;
+// other rows zero gradient.  Result = sum of row losses (0 if none / not finite).
+void oracle_cross_entropy_loss(const uint16_t* logits, const void* tgt, uint16_t* grad, uint16_t* result,
+                               uint32_t rows, uint32_t V, uint32_t target_bytes, int dt) {
+    auto target = [&](uint32_t r) {
+        return target_bytes == 2 ? (uint32_t)((const uint16_t*)tgt)[r] : ((const uint32_t*)tgt)[r];
+    };
+    double count = 0.0;
+    for (uint32_t r = 0; r < rows; ++r) count += (target(r) != 0 && target(r) < V) ? 1.0 : 0.0;
+    std::vector<double> loss(rows, 0.0);
+    par_for((int64_t)rows, [&](int64_t r) {
+        const uint64_t b = (uint64_t)r * V;
+        const uint32_t t = target((uint32_t)r);
+        if (!(t != 0 && t < V && count > 0.0)) {
+            for (uint32_t j = 0; j < V; ++j) grad[b + j] = st(0.0f, dt);
+            return;
+        }
+        auto lv = [&](uint32_t j) { return (double)std::min(std::max(ld(logits, b + j, dt), -65000.0f), 65000.0f); };
+        double mx = -1e300;
+        for (uint32_t j = 0; j < V; ++j) mx = std::max(mx, lv(j));
+        double den = 0.0;
+        for (uint32_t j = 0; j < V; ++j) den += std::exp(lv(j) - mx);
+        den = std::max(den, 1e-20);
+        for (uint32_t j = 0; j < V; ++j) {
+            double gv = std::exp(lv(j) - mx) / den / count;
+            if (j == t) gv -= 1.0 / count;
+            grad[b + j] = st((float)gv, dt);
+        }
+        loss[r] = (mx + std::log(den) - lv(t)) / count;
+    });
+    double s = 0.0;
+    for (uint32_t r = 0; r < rows; ++r) s += loss[r];
+    if (!(count > 0.0) || std::isnan(s) || std::isinf(s)) s = 0.0;
+    result[0] = st((float)s, dt);
+}
+// shaders/flash_attention_bwd.comp (modes 0 and 1), restated per element:
+// s_ij = q_i.k_j * scale, m_i / l_i / t_i the row max, exp-sum and
+// sum_j e^(s_ij - m_i) (dO_i.v_j); p_ij = e^(s_ij - m_i) / l_i;
+// a_ij = (dO_i.v_j - c_i) p_ij scale with c_i = t_i (the shader) or t_i / l_i
+// (flag 2, exact gradient); dQ_i = sum_j a_ij k_j, dK_j = sum_{h,i} a_ij q_i,
+// dV_j = sum_{h,i} p_ij dO_i.  K/V head g serves heads g*H/Hkv ...; flag 1 causal.
+void oracle_flash_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* dO,
+                                uint16_t* dQ, uint16_t* dK, uint16_t* dV, uint32_t B, uint32_t N, uint32_t H,
+                                uint32_t Hkv, uint32_t Dh, float scale, uint32_t flags, int dt) {
+    const bool causal = flags & 1u, normalized = flags & 2u;
+    if (!(scale > 0.0f)) scale = 1.0f / std::sqrt((float)Dh);
+    const uint64_t qp = (uint64_t)H * Dh, kp = (uint64_t)Hkv * Dh;
+    const uint32_t hg = H / Hkv;
+    // per (b, h, i): m, l, c
+    std::vector<double> mm((uint64_t)B * H * N), ll(mm.size()), cc(mm.size());
+    auto S = [&](uint32_t b, uint32_t h, uint32_t i, uint32_t j) {
+        double s = 0.0;
+        const uint32_t g = h / hg;
+        for (uint32_t d = 0; d < Dh; ++d)
+            s += (double)ld(q, (b * (uint64_t)N + i) * qp + h * Dh + d, dt) * ld(k, (b * (uint64_t)N + j) * kp + g * Dh + d, dt);
+        return s * scale;
+    };
+    auto DP = [&](uint32_t b, uint32_t h, uint32_t i, uint32_t j) {
+        double s = 0.0;
+        const uint32_t g = h / hg;
+        for (uint32_t d = 0; d < Dh; ++d)
+            s += (double)ld(dO, (b * (uint64_t)N + i) * qp + h * Dh + d, dt) * ld(v, (b * (uint64_t)N + j) * kp + g * Dh + d, dt);
+        return s;
+    };
+    par_for((int64_t)B * H * N, [&](int64_t x) {
+        const uint32_t i = (uint32_t)(x % N), h = (uint32_t)((x / N) % H), b = (uint32_t)(x / ((int64_t)N * H));
+        const uint32_t je = causal ? i + 1 : N;
+        double m = -1e300;
+        for (uint32_t j = 0; j < je; ++j) m = std::max(m, S(b, h, i, j));
+        double l = 0.0, t = 0.0;
+        for (uint32_t j = 0; j < je; ++j) {
+            const double w = std::exp(S(b, h, i, j) - m);
+            l += w;
+            t += w * DP(b, h, i, j);
+        }
+        mm[x] = m;
+        ll[x] = l;
+        cc[x] = normalized ? t / std::max(l, 1e-20) : t;
+        // dQ
+        for (uint32_t d = 0; d < Dh; ++d) {
+            double acc = 0.0;
+            for (uint32_t j = 0; j < je; ++j) {
+                const double p = std::exp(S(b, h, i, j) - m) / std::max(l, 1e-20);
+                const double a = (DP(b, h, i, j) - cc[x]) * p * scale;
+                acc += a * ld(k, (b * (uint64_t)N + j) * kp + (h / hg) * Dh + d, dt);
+            }
+            dQ[(b * (uint64_t)N + i) * qp + h * Dh + d] = st((float)acc, dt);
+        }
+    });
+    par_for((int64_t)B * Hkv * N, [&](int64_t x) {
+        const uint32_t j = (uint32_t)(x % N), g = (uint32_t)((x / N) % Hkv), b = (uint32_t)(x / ((int64_t)N * Hkv));
+        std::vector<double> ak(Dh, 0.0), av(Dh, 0.0);
+        for (uint32_t hh = 0; hh < hg; ++hh) {
+            const uint32_t h = g * hg + hh;
+            for (uint32_t i = causal ? j : 0; i < N; ++i) {
+                const uint64_t si = ((uint64_t)b * H + h) * N + i;
+                const double p = std::exp(S(b, h, i, j) - mm[si]) / std::max(ll[si], 1e-20);
+                const double a = (DP(b, h, i, j) - cc[si]) * p * scale;
+                for (uint32_t d = 0; d < Dh; ++d) {
+                    ak[d] += a * ld(q, (b * (uint64_t)N + i) * qp + h * Dh + d, dt);
+                    av[d] += p * ld(dO, (b * (uint64_t)N + i) * qp + h * Dh + d, dt);
+                }
+            }
+        }
+        for (uint32_t d = 0; d < Dh; ++d) {
+            dK[(b * (uint64_t)N + j) * kp + g * Dh + d] = st((float)ak[d], dt);
+            dV[(b * (uint64_t)N + j) * kp + g * Dh + d] = st((float)av[d], dt);
+        }
+    });
+}
+
 void oracle_fill_normal(uint16_t* out, uint64_t n, uint64_t seed, float mean, float stddev, int dt) {
     const uint64_t s0 = splitmix(seed);
     par_for((int64_t)n, [&](int64_t i) {

@@ -54,6 +54,34 @@ void oracle_embed(const uint16_t* E, const void* idx, uint16_t* out, uint32_t vo
 void oracle_greedy_sample(const uint16_t* logits, void* out, uint32_t B, uint32_t S, uint32_t V, uint32_t position,
                           uint32_t token_base, uint32_t token_count, uint32_t out_bytes, int dtype);
 
+/* training side (shaders cited in evk_oracle.cpp) */
+void oracle_relu(const uint16_t* in, uint16_t* out, uint64_t n, int dtype);
+void oracle_relu_backward(const uint16_t* go, const uint16_t* in, uint16_t* gi, uint64_t n, int dtype);
+void oracle_gelu_backward(const uint16_t* go, const uint16_t* in, uint16_t* gi, uint64_t n, int dtype);
+void oracle_softmax_backward(const uint16_t* p, const uint16_t* g, uint16_t* gi, uint32_t rows, uint32_t L,
+                             float scale, int dtype);
+void oracle_rms_norm_backward(const uint16_t* x, const uint16_t* g, uint16_t* gi, uint32_t rows, uint32_t D,
+                              float eps, int dtype);
+void oracle_rope_backward(const uint16_t* go, uint16_t* gi, uint32_t batch, uint32_t seq_len, uint32_t dim,
+                          float base, int dtype);
+void oracle_embed_backward(const uint16_t* go, const void* idx, uint16_t* gE, uint32_t vocab, uint32_t dim,
+                           uint32_t n_idx, uint32_t idx_bytes, int dtype);
+void oracle_position_add(const uint16_t* in, const uint16_t* pos, uint16_t* out, uint32_t batch, uint32_t seq_len,
+                         uint32_t dim, int dtype);
+void oracle_position_add_backward(const uint16_t* go, uint16_t* gi, uint16_t* gp, uint32_t batch, uint32_t seq_len,
+                                  uint32_t dim, int dtype);
+void oracle_sum_batch(const uint16_t* in, uint16_t* out, uint32_t batch, uint64_t size, int dtype);
+void oracle_sgd(uint16_t* p, const uint16_t* g, uint64_t n, float lr, int dtype);
+void oracle_adam(uint16_t* p, const uint16_t* g, uint16_t* m, uint16_t* v, uint64_t n, uint32_t step, float lr,
+                 float beta1, float beta2, float eps, int dtype);
+void oracle_mse_loss(const uint16_t* pred, const uint16_t* tgt, uint16_t* grad, uint16_t* result, uint64_t n,
+                     int dtype);
+void oracle_cross_entropy_loss(const uint16_t* logits, const void* tgt, uint16_t* grad, uint16_t* result,
+                               uint32_t rows, uint32_t V, uint32_t target_bytes, int dtype);
+void oracle_flash_attention_bwd(const uint16_t* q, const uint16_t* k, const uint16_t* v, const uint16_t* dO,
+                                uint16_t* dQ, uint16_t* dK, uint16_t* dV, uint32_t B, uint32_t N, uint32_t H,
+                                uint32_t Hkv, uint32_t Dh, float scale, uint32_t flags, int dtype);
+
 /* Seeded generator shared by tests, bench and fixtures (portable, unlike the
  * reference's libc rand()): splitmix64 stream -> Box-Muller normals. */
 void oracle_fill_normal(uint16_t* out, uint64_t n, uint64_t seed, float mean, float stddev, int dtype);

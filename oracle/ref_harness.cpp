@@ -4,12 +4,10 @@
 //
 // It supplies (1) the evk core functions that evk_ai.h / tests.h use, on host
 // memory (commands execute at record time; submit/wait are no-ops), and (2)
-// the evk::ai operators through the same shape logic as the product
-// (evk_b200/cpp/evk_ai_dispatch.h) with the oracle as the backend.  The
-// reference's training-side operators are outside this backend's scope; the
-// backward passes that the forward tests also exercise (gelu, rope, rms_norm,
-// embed) get small host implementations here so those tests run to the end,
-// and the remaining ones abort if a selected test ever reaches them.
+// the evk::ai operators, inference and training side, through the same shape
+// logic as the product (evk_b200/cpp/evk_ai_dispatch.h) with the oracle as
+// the backend, so the reference's known-answer tests pin every oracle
+// restatement the GPU parity tests compare against.
 #include <chrono>
 #include <cstring>
 #include <type_traits>
@@ -136,13 +134,77 @@ int o_greedy(const void* l, void* out, uint32_t B, uint32_t S, uint32_t V, uint3
     oracle_greedy_sample((const u16*)l, out, B, S, V, pos, base, cnt, ob, dt);
     return 0;
 }
-const evk_b200::Backend kOracle = {no_stream, die,     o_matmul, o_flash, o_sqa,  o_rms,   o_rope,  o_gelu,
-                                   o_softmax, o_add,   o_scale,  o_zero,  o_mask, o_embed, o_greedy};
-
-[[noreturn]] void out_of_scope(const char* op) {
-    std::fprintf(stderr, "oracle harness: %s is a training-side operator outside this backend\n", op);
-    std::exit(3);
+// training side
+int o_relu(const void* in, void* out, uint64_t n, int dt, void*) {
+    oracle_relu((const u16*)in, (u16*)out, n, dt);
+    return 0;
 }
+int o_relu_bwd(const void* go, const void* in, void* gi, uint64_t n, int dt, void*) {
+    oracle_relu_backward((const u16*)go, (const u16*)in, (u16*)gi, n, dt);
+    return 0;
+}
+int o_gelu_bwd(const void* go, const void* in, void* gi, uint64_t n, int dt, void*) {
+    oracle_gelu_backward((const u16*)go, (const u16*)in, (u16*)gi, n, dt);
+    return 0;
+}
+int o_softmax_bwd(const void* p, const void* g, void* gi, uint32_t rows, uint32_t L, float s, int dt, void*) {
+    oracle_softmax_backward((const u16*)p, (const u16*)g, (u16*)gi, rows, L, s, dt);
+    return 0;
+}
+int o_rms_bwd(const void* x, const void* g, void* gi, uint32_t rows, uint32_t D, float eps, int dt, void*) {
+    oracle_rms_norm_backward((const u16*)x, (const u16*)g, (u16*)gi, rows, D, eps, dt);
+    return 0;
+}
+int o_rope_bwd(const void* go, void* gi, uint32_t b, uint32_t s, uint32_t d, float base, int dt, void*) {
+    oracle_rope_backward((const u16*)go, (u16*)gi, b, s, d, base, dt);
+    return 0;
+}
+int o_embed_bwd(const void* go, const void* idx, void* gE, uint32_t V, uint32_t D, uint32_t n, uint32_t ib, int dt,
+                void*) {
+    oracle_embed_backward((const u16*)go, idx, (u16*)gE, V, D, n, ib, dt);
+    return 0;
+}
+int o_pos_add(const void* in, const void* pos, void* out, uint32_t b, uint32_t s, uint32_t d, int dt, void*) {
+    oracle_position_add((const u16*)in, (const u16*)pos, (u16*)out, b, s, d, dt);
+    return 0;
+}
+int o_pos_add_bwd(const void* go, void* gi, void* gp, uint32_t b, uint32_t s, uint32_t d, int dt, void*) {
+    oracle_position_add_backward((const u16*)go, (u16*)gi, (u16*)gp, b, s, d, dt);
+    return 0;
+}
+int o_sum_batch(const void* in, void* out, uint32_t batch, uint64_t size, int dt, void*) {
+    oracle_sum_batch((const u16*)in, (u16*)out, batch, size, dt);
+    return 0;
+}
+int o_sgd(void* p, const void* g, uint64_t n, float lr, int dt, void*) {
+    oracle_sgd((u16*)p, (const u16*)g, n, lr, dt);
+    return 0;
+}
+int o_adam(void* p, const void* g, void* m, void* v, uint64_t n, uint32_t step, float lr, float b1, float b2, float eps,
+           int dt, void*) {
+    oracle_adam((u16*)p, (const u16*)g, (u16*)m, (u16*)v, n, step, lr, b1, b2, eps, dt);
+    return 0;
+}
+int o_mse(const void* p, const void* t, void* g, void* r, uint64_t n, int dt, void*) {
+    oracle_mse_loss((const u16*)p, (const u16*)t, (u16*)g, (u16*)r, n, dt);
+    return 0;
+}
+int o_ce(const void* l, const void* t, void* g, void* r, uint32_t rows, uint32_t V, uint32_t tb, int dt, void*) {
+    oracle_cross_entropy_loss((const u16*)l, t, (u16*)g, (u16*)r, rows, V, tb, dt);
+    return 0;
+}
+int o_flash_bwd(const void* q, const void* k, const void* v, const void*, const void* dO, void* dQ, void* dK, void* dV,
+                uint32_t B, uint32_t N, uint32_t H, uint32_t Hkv, uint32_t Dh, float scale, uint32_t flags, int dt,
+                void*) {
+    oracle_flash_attention_bwd((const u16*)q, (const u16*)k, (const u16*)v, (const u16*)dO, (u16*)dQ, (u16*)dK,
+                               (u16*)dV, B, N, H, Hkv, Dh, scale, flags, dt);
+    return 0;
+}
+const evk_b200::Backend kOracle = {
+    no_stream, die,          o_matmul,   o_flash,   o_sqa,       o_rms,         o_rope,       o_gelu,
+    o_softmax, o_add,        o_scale,    o_zero,    o_mask,      o_embed,       o_greedy,     o_relu,
+    o_relu_bwd, o_gelu_bwd,  o_softmax_bwd, o_rms_bwd, o_rope_bwd, o_embed_bwd,  o_pos_add,    o_pos_add_bwd,
+    o_sum_batch, o_sgd,      o_adam,     o_mse,     o_ce,        o_flash_bwd};
 }  // namespace
 
 namespace evk::ai {
@@ -173,82 +235,65 @@ void scale(Tensor& t, float s) { evk_b200::scale(kOracle, t, s); }
 void zero(Tensor& t) { evk_b200::zero(kOracle, t); }
 void rms_norm(Tensor& in, Tensor& out, float eps) { evk_b200::rms_norm(kOracle, in, out, eps); }
 
-// --- backward passes used by the forward tests (host math, test-only) ---
-void gelu_backward(Tensor& grad_out, Tensor& in, Tensor& grad_in) {
-    auto* go = (float16_t*)grad_out.buffer.GetPtr();
-    auto* x = (float16_t*)in.buffer.GetPtr();
-    auto* gi = (float16_t*)grad_in.buffer.GetPtr();
-    for (uint32_t i = 0; i < in.shape.count(); ++i) gi[i] = float16_t(float(gi[i]) + float(go[i]) * gelu_grad_approx_cpu(float(x[i])));
+// --- training side ---
+void AdamState::init(uint32_t n) {
+    m_buffer = evk::CreateBuffer({.size = (uint64_t)n * sizeof(float16_t)});
+    v_buffer = evk::CreateBuffer({.size = (uint64_t)n * sizeof(float16_t)});  // host memory, zero-filled
+    t = 0;
 }
-void rope_backward(Tensor& grad_out, Tensor& grad_in, uint32_t B, uint32_t S, uint32_t D, float base) {
-    auto* go = (float16_t*)grad_out.buffer.GetPtr();
-    auto* gi = (float16_t*)grad_in.buffer.GetPtr();
-    for (uint32_t r = 0; r < B * S; ++r)
-        for (uint32_t p = 0; p < D / 2; ++p) {
-            float ang = float(r % S) * std::pow(base, -2.0f * float(p) / float(D));
-            float c = std::cos(ang), s = std::sin(ang);
-            float g0 = go[r * D + 2 * p], g1 = go[r * D + 2 * p + 1];
-            gi[r * D + 2 * p] = float16_t(float(gi[r * D + 2 * p]) + g0 * c + g1 * s);
-            gi[r * D + 2 * p + 1] = float16_t(float(gi[r * D + 2 * p + 1]) - g0 * s + g1 * c);
-        }
+void AdamState::reset() {
+    m_buffer = {};
+    v_buffer = {};
+    t = 0;
 }
-void rms_norm_backward(Tensor& in, Tensor& grad_out, Tensor& grad_in, float eps) {
-    auto* x = (float16_t*)in.buffer.GetPtr();
-    auto* go = (float16_t*)grad_out.buffer.GetPtr();
-    auto* gi = (float16_t*)grad_in.buffer.GetPtr();
-    const uint32_t D = in.shape[-1], rows = in.shape.count() / D;
-    for (uint32_t r = 0; r < rows; ++r) {
-        float ss = 0.0f;
-        for (uint32_t d = 0; d < D; ++d) ss += float(x[r * D + d]) * float(x[r * D + d]);
-        const float inv = 1.0f / std::sqrt(ss / float(D) + eps);
-        float dot = 0.0f;
-        for (uint32_t d = 0; d < D; ++d) dot += float(go[r * D + d]) * float(x[r * D + d]) * inv;
-        for (uint32_t d = 0; d < D; ++d) {
-            const float y = float(x[r * D + d]) * inv;
-            gi[r * D + d] = float16_t(float(gi[r * D + d]) + (float(go[r * D + d]) - y * dot / float(D)) * inv);
-        }
-    }
+void flash_attention_bwd(Tensor& q, Tensor& k, Tensor& v, Tensor& o, Tensor& dO, Tensor& dQ, Tensor& dK, Tensor& dV,
+                         uint32_t heads) {
+    evk_b200::flash_attention_bwd(kOracle, q, k, v, o, dO, dQ, dK, dV, heads);
 }
-void embed_backward(Tensor& grad_out, Tensor& idx, Tensor& grad_E) {
-    auto* go = (float16_t*)grad_out.buffer.GetPtr();
-    auto* ids = (uint16_t*)idx.buffer.GetPtr();
-    auto* ge = (float16_t*)grad_E.buffer.GetPtr();
-    const uint32_t D = grad_E.shape[1];
-    for (uint32_t i = 0; i < idx.shape.count(); ++i)
-        for (uint32_t d = 0; d < D; ++d) ge[ids[i] * D + d] = float16_t(float(ge[ids[i] * D + d]) + float(go[i * D + d]));
+void mse_loss(Tensor& p, Tensor& t, Tensor& g, Tensor& r) { evk_b200::mse_loss(kOracle, p, t, g, r); }
+void sgd(Tensor& p, Tensor& g, float lr) { evk_b200::sgd(kOracle, p, g, lr); }
+void adam(Tensor& p, Tensor& g, AdamState& st, float lr, float b1, float b2, float eps) {
+    if (!st.m_buffer) st.init(p.shape.count());
+    st.t += 1;
+    evk_b200::adam(kOracle, p, g, st.m_buffer.GetPtr(), st.v_buffer.GetPtr(), st.t, lr, b1, b2, eps);
 }
-
-// --- training-side operators: outside this backend ---
-void AdamState::init(uint32_t) { out_of_scope("AdamState::init"); }
-void AdamState::reset() {}
-void flash_attention_bwd(Tensor&, Tensor&, Tensor&, Tensor&, Tensor&, Tensor&, Tensor&, Tensor&, uint32_t) { out_of_scope("flash_attention_bwd"); }
-void mse_loss(Tensor&, Tensor&, Tensor&, Tensor&) { out_of_scope("mse_loss"); }
-void sgd(Tensor&, Tensor&, float) { out_of_scope("sgd"); }
-void adam(Tensor&, Tensor&, AdamState&, float, float, float, float) { out_of_scope("adam"); }
-void softmax_backward(Tensor&, Tensor&, Tensor&, float) { out_of_scope("softmax_backward"); }
-void relu(Tensor&, Tensor&) { out_of_scope("relu"); }
-void relu_backward(Tensor&, Tensor&, Tensor&) { out_of_scope("relu_backward"); }
-void cross_entropy_loss(Tensor&, Tensor&, Tensor&, Tensor&) { out_of_scope("cross_entropy_loss"); }
-void position_add(Tensor&, Tensor&, Tensor&, uint32_t, uint32_t, uint32_t) { out_of_scope("position_add"); }
-void position_add_backward(Tensor&, Tensor&, Tensor&, uint32_t, uint32_t, uint32_t) { out_of_scope("position_add_backward"); }
-void sum_batch(Tensor&, Tensor&, uint32_t, uint32_t) { out_of_scope("sum_batch"); }
+void softmax_backward(Tensor& p, Tensor& go, Tensor& gi, float s) { evk_b200::softmax_backward(kOracle, p, go, gi, s); }
+void relu(Tensor& in, Tensor& out) { evk_b200::relu(kOracle, in, out); }
+void relu_backward(Tensor& go, Tensor& in, Tensor& gi) { evk_b200::relu_backward(kOracle, go, in, gi); }
+void gelu_backward(Tensor& go, Tensor& in, Tensor& gi) { evk_b200::gelu_backward(kOracle, go, in, gi); }
+void cross_entropy_loss(Tensor& l, Tensor& t, Tensor& g, Tensor& r) { evk_b200::cross_entropy_loss(kOracle, l, t, g, r); }
+void embed_backward(Tensor& go, Tensor& idx, Tensor& gE) { evk_b200::embed_backward(kOracle, go, idx, gE); }
+void position_add(Tensor& in, Tensor& pos, Tensor& out, uint32_t B, uint32_t S, uint32_t D) {
+    evk_b200::position_add(kOracle, in, pos, out, B, S, D);
+}
+void position_add_backward(Tensor& go, Tensor& gi, Tensor& gp, uint32_t B, uint32_t S, uint32_t D) {
+    evk_b200::position_add_backward(kOracle, go, gi, gp, B, S, D);
+}
+void rope_backward(Tensor& go, Tensor& gi, uint32_t B, uint32_t S, uint32_t D, float base) {
+    evk_b200::rope_backward(kOracle, go, gi, B, S, D, base);
+}
+void sum_batch(Tensor& in, Tensor& out, uint32_t b, uint32_t size) { evk_b200::sum_batch(kOracle, in, out, b, size); }
+void rms_norm_backward(Tensor& in, Tensor& go, Tensor& gi, float eps) {
+    evk_b200::rms_norm_backward(kOracle, in, go, gi, eps);
+}
 }  // namespace evk::ai
 
 int main(int argc, char** argv) {
-    // The inference-path known-answer tests of example/tests.h.  The
-    // 32768-token flash-vs-unfused comparison runs only with --flash (it
-    // materialises two 2 GB score matrices on the host).
+    // Every test of example/tests.h: the reference's default list
+    // (run_ai_kernel_tests, tests.h:1565-1585) and the ones it leaves out,
+    // except test_adam_batched_matmul: it steps Adam with lr = -0.02
+    // (tests.h:1009) on the mse_loss gradient 2 (pred - target) / n, which
+    // climbs the loss under the reference's own update rule
+    // (shaders/adam.comp: param -= lr * update), so it cannot pass on any
+    // faithful backend.  The 32768-token flash-vs-unfused comparison runs only
+    // with --flash (it materialises two 2 GB score matrices on the host).
     bool flash = argc > 1 && std::strcmp(argv[1], "--flash") == 0;
-    test_add();
-    test_matmul();
-    test_matmul_broadcast();
-    test_softmax();
-    test_gelu();
-    test_scale_zero();
-    test_embed_and_backward();
-    test_rope_and_backward();
-    test_rms_norm_and_backward();
-    test_greedy_sample();
+    run_ai_kernel_tests();
+    test_flash_attention_backward();
+    test_graph_backward();
+    test_attn_graph();
+    test_adam_convergence();
+    test_adam_vs_sgd();
     if (flash) test_flash_attention_cmp_softmax();
     std::printf("ALL REFERENCE KATS PASSED (oracle backend)\n");
     return 0;
