@@ -48,6 +48,15 @@ static const evk_b200::Backend& backend() {
     return be;
 }
 
+}  // namespace evk::ai
+
+namespace evk_b200 {
+// The backend table, shared with the extensions (evk_ai_ext.cpp).
+const Backend& cpp_backend() { return evk::ai::backend(); }
+}  // namespace evk_b200
+
+namespace evk::ai {
+
 void initialize() {
     if (evkcu_init(-1) != EVKCU_OK) fatal(EVKCU_CUDA_ERROR, "initialize");
 }

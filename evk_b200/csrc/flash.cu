@@ -40,10 +40,15 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when th
 //             sub-partition, so one tile's exponentials overlap the others'
 //             row max, P store and barrier waits.
 //   Dh = 128: two tiles over 128-key blocks.
-template <int DH, int NT, int FN_, int POLY_ = 0>
+template <int DH, int NT, int FN_, int POLY_ = 0, bool QT_ = false>
 struct FlashCfg {
     static constexpr int FN = FN_;    // keys per block
     static constexpr int POLY = POLY_;
+    // Q in TMEM: the softmax warps store their Q rows into TMEM once per
+    // item and the S MMA reads its A operand from there (A from shared
+    // memory costs a 128 x 16 operand fetch per MMA: 102 vs 73 clocks for
+    // M = 128, N = 128, K = 16, measured).
+    static constexpr bool QT = QT_;
     static constexpr int Q_BYTES = FM * DH * 2;  // per tile
     static constexpr int KV_BYTES = FN * DH * 2;  // one K or V block
     static constexpr int STAGES = NT == 4 ? 8 : NT == 2 ? (DH == 64 ? 5 : 2) : (DH == 64 ? 6 : 3);
@@ -53,21 +58,23 @@ struct FlashCfg {
     // values packed two per column, FN/2 columns).  When the three do not fit
     // the tile's share of TMEM, P is written over the tile's S, and S_t(j + 1)
     // waits until PV_t(j) has read it.
-    static constexpr bool ALIAS_P = FN + DH + FN / 2 > TSTRIDE;
-    static_assert(FN + DH <= TSTRIDE, "S and O must fit the tile's TMEM share");
+    static constexpr int QCOLS = QT ? DH / 2 : 0;  // Q as packed 16-bit pairs
+    static constexpr bool ALIAS_P = FN + DH + FN / 2 + QCOLS > TSTRIDE;
+    static_assert(FN + DH + QCOLS <= TSTRIDE, "S, O (and Q) must fit the tile's TMEM share");
     static constexpr int OFF_Q = 0;
-    static constexpr int OFF_K = OFF_Q + NT * Q_BYTES;
+    static constexpr int OFF_K = OFF_Q + (QT ? 0 : NT * Q_BYTES);
     static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
     static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
-    static constexpr int BAR_BYTES = ((2 + 3 * STAGES + 5 * NT) * 8 + 16 + 127) / 128 * 128;
+    static constexpr int BAR_BYTES = ((2 + 3 * STAGES + 6 * NT) * 8 + 16 + 127) / 128 * 128;
     static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
     static constexpr int THREADS = 128 + NT * 128;
     static __device__ __forceinline__ uint32_t col_s(int t) { return t * TSTRIDE; }
     static __device__ __forceinline__ uint32_t col_o(int t) { return t * TSTRIDE + FN; }
     static __device__ __forceinline__ uint32_t col_p(int t) { return ALIAS_P ? t * TSTRIDE : t * TSTRIDE + FN + DH; }
+    static __device__ __forceinline__ uint32_t col_q(int t) { return t * TSTRIDE + FN + DH; }
 };
 static_assert(FlashCfg<64, 2, 128>::SMEM <= 227 * 1024 && FlashCfg<128, 2, 128>::SMEM <= 227 * 1024 &&
-                  FlashCfg<64, 4, 64>::SMEM <= 227 * 1024,
+                  FlashCfg<64, 4, 64>::SMEM <= 227 * 1024 && FlashCfg<64, 2, 128, 0, true>::SMEM <= 227 * 1024,
               "flash smem");
 
 // max(a, b, c) in one instruction (sm_100).
@@ -153,7 +160,8 @@ __device__ __forceinline__ float2 ex2_poly2(float2 x) {
 template <typename T, typename Cfg, int DH, int NT>
 __global__ void __launch_bounds__(Cfg::THREADS, 1)
     flash_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, T* __restrict__ O, uint32_t N, uint32_t H,
+                    const __grid_constant__ CUtensorMap tmV, const T* __restrict__ Qg, T* __restrict__ O, uint32_t N,
+                    uint32_t H,
                     uint32_t Hkv, uint32_t BH, float scale_log2, int causal, uint32_t idesc_s, uint32_t idesc_pv,
                     unsigned int* err) {
     constexpr int ST = Cfg::STAGES;
@@ -177,7 +185,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     uint64_t* p_full = s_free + NT;     // [NT]
     uint64_t* pv_done = p_full + NT;    // [NT]
     uint64_t* o_free = pv_done + NT;    // [NT]
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(o_free + NT);
+    uint64_t* q_tm = o_free + NT;       // [NT] Q_t stored in TMEM (Cfg::QT)
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(q_tm + NT);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -220,6 +229,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             mbar_init(&p_full[t], 4);
             mbar_init(&pv_done[t], 1);
             mbar_init(&o_free[t], 4);
+            mbar_init(&q_tm[t], 4);
         }
         *s_abort = 0;
         fence_barrier_init();
@@ -254,18 +264,20 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
 #pragma unroll
                 for (int t = 0; t < NT; ++t) nmax = max(nmax, nblk[t]);
                 const uint32_t g = h / (H / Hkv);
-                // Q buffer is free once the previous item's S MMAs completed.
-                if (it > 0 && !mbar_wait(q_empty, (it - 1) & 1, s_abort, err, kTimeoutFlash)) {
-                    ok = false;
-                    break;
+                if constexpr (!Cfg::QT) {
+                    // Q buffer is free once the previous item's S MMAs completed.
+                    if (it > 0 && !mbar_wait(q_empty, (it - 1) & 1, s_abort, err, kTimeoutFlash)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(q_full, NT * Cfg::Q_BYTES);
+#pragma unroll
+                    for (int t = 0; t < NT; ++t)
+#pragma unroll
+                        for (int c = 0; c < DH / 64; ++c)
+                            tma_load_3d(sQ + t * Cfg::Q_BYTES + c * FM * 128, &tmQ, q_full, (int)(h * DH + c * 64),
+                                        (int)q0[t], (int)b);
                 }
-                mbar_arrive_expect_tx(q_full, NT * Cfg::Q_BYTES);
-#pragma unroll
-                for (int t = 0; t < NT; ++t)
-#pragma unroll
-                    for (int c = 0; c < DH / 64; ++c)
-                        tma_load_3d(sQ + t * Cfg::Q_BYTES + c * FM * 128, &tmQ, q_full, (int)(h * DH + c * 64),
-                                    (int)q0[t], (int)b);
                 ++it;
                 for (uint32_t j = 0; j < nmax; ++j, ++r) {
                     const int st = r % ST;
@@ -315,7 +327,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             uint32_t nmax = 0;
 #pragma unroll
             for (int t = 0; t < NT; ++t) nmax = max(nmax, nblk[t]);
-            if (is_s && !probe(lane == 0 && mbar_wait(q_full, it & 1, s_abort, err, kTimeoutFlash))) break;
+            if (!Cfg::QT && is_s && !probe(lane == 0 && mbar_wait(q_full, it & 1, s_abort, err, kTimeoutFlash)))
+                break;
             tc_fence_after();
             for (uint32_t j = 0; ok && j < nmax; ++j) {
                 const uint32_t r = rbase + j;
@@ -331,15 +344,24 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                         // must have read P (which also implies the former).
                         ok = gj == 0 || probe(lane == 0 && mbar_wait(&s_reuse[t], (gj - 1) & 1, s_abort, err,
                                                                      kTimeoutFlash));
+                        // Q in TMEM: the first S of an item waits until
+                        // softmax t has stored the item's Q rows.
+                        if (Cfg::QT && ok && j == 0)
+                            ok = probe(lane == 0 && mbar_wait(&q_tm[t], ep[t] & 1, s_abort, err, kTimeoutFlash));
                         if (!ok) break;
                         tc_fence_after();
                         if (leader) {
 #pragma unroll
                             for (int kk = 0; kk < DH / 16; ++kk) {
-                                uint64_t ad = make_sw128_desc(
-                                    qaddr + t * Cfg::Q_BYTES + (kk >> 2) * (FM * 128) + (kk & 3) * 32, 16, 1024);
                                 uint64_t bd = make_sw128_desc(kaddr + (kk >> 2) * (FN * 128) + (kk & 3) * 32, 16, 1024);
-                                mma_f16_ss(tmem + Cfg::col_s(t), ad, bd, idesc_s, kk != 0);
+                                if constexpr (Cfg::QT) {
+                                    mma_f16_ts(tmem + Cfg::col_s(t), tmem + Cfg::col_q(t) + kk * 8, bd, idesc_s,
+                                               kk != 0);
+                                } else {
+                                    uint64_t ad = make_sw128_desc(
+                                        qaddr + t * Cfg::Q_BYTES + (kk >> 2) * (FM * 128) + (kk & 3) * 32, 16, 1024);
+                                    mma_f16_ss(tmem + Cfg::col_s(t), ad, bd, idesc_s, kk != 0);
+                                }
                             }
                             mma_commit(&s_full[t]);
                         }
@@ -347,7 +369,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                     }
                     if (!ok) break;
                     // Q is free once every S of this item has completed.
-                    if (j + 1 == nmax && leader) mma_commit(q_empty);
+                    if (!Cfg::QT && j + 1 == nmax && leader) mma_commit(q_empty);
                 } else {
                     ok = probe(lane == 0 && mbar_wait(&v_full[r % ST], (r / ST) & 1, s_abort, err, kTimeoutFlash));
                     const uint32_t vaddr = smem_u32(sV + (r % ST) * Cfg::KV_BYTES);
@@ -408,6 +430,31 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             if (nb == 0) continue;
             const uint32_t qidx = q0[t] + row;
             const uint32_t kmax = min(N, causal ? qidx + 1 : N);  // keys < kmax are valid
+            if constexpr (Cfg::QT) {
+                // This row of Q_t into TMEM (16-bit pairs, the MMA's A
+                // layout).  Every S MMA of the previous item has completed:
+                // this warp consumed them all.
+                uint32_t qw[DH / 2];
+                const uint4* src = reinterpret_cast<const uint4*>(
+                    Qg + ((uint64_t)b * N + (qidx < N ? qidx : 0)) * ((uint64_t)H * DH) + (uint64_t)h * DH);
+#pragma unroll
+                for (int c = 0; c < DH / 8; ++c) {
+                    const uint4 v = qidx < N ? src[c] : make_uint4(0u, 0u, 0u, 0u);
+                    qw[4 * c] = v.x;
+                    qw[4 * c + 1] = v.y;
+                    qw[4 * c + 2] = v.z;
+                    qw[4 * c + 3] = v.w;
+                }
+#pragma unroll
+                for (int c = 0; c < DH / 64; ++c) {
+                    uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t (*)[32]>(qw + 32 * c);
+                    tmem_st32(lane_addr + Cfg::col_q(t) + 32 * c, chunk);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&q_tm[t]);
+            }
             float m_ref = -INFINITY, l = 0.0f;
             for (uint32_t j = 0; j < nb; ++j) {
                 const uint32_t gj = gbase + j;
@@ -625,10 +672,10 @@ __global__ void __launch_bounds__(256) flash_simt_kernel(const T* __restrict__ Q
     }
 }
 
-template <typename T, int DH, int NT, int FN, int POLY>
+template <typename T, int DH, int NT, int FN, int POLY, bool QT = false>
 int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N, uint32_t H,
                     uint32_t Hkv, float scale_log2, int causal, int dtype, uint64_t kv_bstride, cudaStream_t st) {
-    using Cfg = FlashCfg<DH, NT, FN, POLY>;
+    using Cfg = FlashCfg<DH, NT, FN, POLY, QT>;
     CUtensorMap mQ, mK, mV;
     int r;
     if ((r = make_tmap_3d(&mQ, q, (uint64_t)H * DH, N, B, (uint64_t)H * DH, (uint64_t)N * H * DH, 64, FM, dtype))) return r;
@@ -657,7 +704,8 @@ int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32
     const uint32_t qtiles = (N + FM - 1) / FM;
     const uint64_t items = (uint64_t)B * H * ((qtiles + NT - 1) / NT);
     const unsigned grid = (unsigned)std::min<uint64_t>(items, (uint64_t)state()->sm_count);
-    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(mQ, mK, mV, (T*)o, N, H, Hkv, B * H, scale_log2, causal, idesc_s,
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM, st>>>(mQ, mK, mV, (const T*)q, (T*)o, N, H, Hkv, B * H, scale_log2, causal,
+                                                idesc_s,
                                                 idesc_pv, state()->d_error);
     return after_launch("evkcu_flash_attention(tcgen05)");
 }
@@ -714,6 +762,12 @@ int flash_attention_kv_strided(const void* q, const void* k, const void* v, void
                     case 3:
                         return launch_flash_tc<T, 64, 4, 64, 4>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype,
                                                                 kv_bstride, st);
+                    case 4:
+                        return launch_flash_tc<T, 64, 2, 128, 0, true>(q, k, v, o, B, N, H, Hkv, scale_log2, causal,
+                                                                       dtype, kv_bstride, st);
+                    case 5:
+                        return launch_flash_tc<T, 64, 2, 128, 2, true>(q, k, v, o, B, N, H, Hkv, scale_log2, causal,
+                                                                       dtype, kv_bstride, st);
                     default:
                         return launch_flash_tc<T, 64, 2, 128, 0>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype,
                                                                  kv_bstride, st);

@@ -97,7 +97,62 @@ def test_graph_causal_attention_eval_backward_vs_oracle(tmp_path, B, N, D):
     r = _graph_oracle(q, k, v, tgt, B, N, D)
     assert_close(o, r[0], 0, what="Graph out")
     assert_close(loss, r[1], 0, rel_l2=2e-3, what="Graph loss")
-    # gradients go through two more fp16-stored intermediates (dP, dS)
-    for g, rr, name in ((dq, r[2], "dq"), (dk, r[3], "dk"), (dv, r[4], "dv")):
-        assert_close(g, rr, 0, rel_l2=5e-3, what=f"Graph {name}")
+    # dv goes through one more fp16-stored tensor (dout).  dq and dk also go
+    # through dP and dS = p (dP - sum p dP), whose cancellation turns a
+    # 1-ulp difference in a stored dP into a larger relative one: 3e-2.
+    assert_close(dv, r[4], 0, rel_l2=5e-3, what="Graph dv")
+    for g, rr, name in ((dq, r[2], "dq"), (dk, r[3], "dk")):
+        assert_close(g, rr, 0, rel_l2=3e-2, what=f"Graph {name}")
     assert_close(q2, r[5], 0, rel_l2=1e-3, what="q after Graph::step")
+
+
+EXT = os.path.join(ROOT, "evk_b200", "reftests", "ext_check")
+
+
+@pytest.mark.skipif(not os.path.exists(EXT), reason="ext_check not built")
+def test_cpp_extensions_vs_oracle(tmp_path):
+    """evk_ai_ext.h through libevk_ai.so (shapes in ext_check.cpp) against the
+    oracle: bf16 GQA causal flash attention, decode attention, per-head RoPE
+    with an offset, RMSNorm with a gain, and 32-bit ids for a 70,000-token
+    vocabulary (embed and greedy_sample, bit-exact)."""
+    bf = 1
+    q1, k1, v1 = oracle.normal(160 * 256, 41, dtype=bf), oracle.normal(160 * 128, 42, dtype=bf), \
+        oracle.normal(160 * 128, 43, dtype=bf)
+    q2, kc, vc = oracle.normal(2 * 256, 44, dtype=bf), oracle.normal(2 * 100 * 128, 45, dtype=bf), \
+        oracle.normal(2 * 100 * 128, 46, dtype=bf)
+    x3 = oracle.normal(2 * 5 * 256, 47, dtype=bf)
+    x4, g4 = oracle.normal(6 * 256, 48, dtype=bf), oracle.normal(256, 49, dtype=bf)
+    E5 = oracle.normal(70000 * 16, 50)
+    ids5 = oracle.uniform_ids(10, 51, 0, 70000, 4)
+    l6 = oracle.normal(2 * 70000, 52, 3.0)
+    fin, fout = tmp_path / "in.bin", tmp_path / "out.bin"
+    with open(fin, "wb") as f:
+        for a in (q1, k1, v1, q2, kc, vc, x3, x4, g4, E5, ids5.view(np.uint16), l6):
+            f.write(np.ascontiguousarray(a).tobytes())
+    rc, out = _run([EXT, str(fin), str(fout)], timeout=300)
+    assert rc == 0 and "EXT_OK" in out, out[-3000:]
+    got = np.fromfile(fout, np.uint16)
+    sizes = [160 * 256, 2 * 256, 2 * 5 * 256, 6 * 256, 10 * 16, 4]
+    assert got.size == sum(sizes)
+    parts, o = [], 0
+    for s in sizes:
+        parts.append(got[o:o + s])
+        o += s
+    r1 = np.empty_like(q1)
+    oracle.flash_attention(q1, k1, v1, r1, 1, 160, 4, 2, 64, 0.0, 1, bf)
+    assert_close(parts[0], r1, bf, rel_l2=8e-3, what="flash_attention_ex")
+    r2 = np.empty_like(q2)
+    oracle.single_query_attention(q2, kc, vc, r2, 2, 4, 2, 64, 100, 77, 0.0, bf)
+    assert_close(parts[1], r2, bf, rel_l2=4e-3, what="single_query_attention")
+    r3 = np.empty_like(x3)
+    oracle.rope(x3, r3, 2, 5, 256, 64, 11, 10000.0, bf)
+    assert_close(parts[2], r3, bf, rel_l2=4e-3, what="rope_ex")
+    r4 = np.empty_like(x4)
+    oracle.rms_norm(x4, r4, 6, 256, 1e-5, gamma=g4, dtype=bf)
+    assert_close(parts[3], r4, bf, rel_l2=4e-3, what="rms_norm_ex")
+    r5 = np.empty(10 * 16, np.uint16)
+    oracle.embed(E5, ids5, r5, 70000, 16)
+    assert np.array_equal(parts[4], r5), "embed_ex with 32-bit ids"
+    r6 = np.zeros(2, np.uint32)
+    oracle.greedy_sample(l6, r6, 2, 1, 70000, 0, 0, 70000, 0)
+    assert np.array_equal(parts[5].view(np.uint32), r6), "greedy_sample_ex with 32-bit ids"
