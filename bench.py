@@ -501,7 +501,7 @@ def main():
             torch.distributed.broadcast(uid, 0)
             comm = evk.Comm(bytes(uid.cpu().numpy()), rank, ws)
         llm = {}
-        for name in (["C3_tiny"] if ws == 1 else []) + ["C4_1.3B", "C5_8B_shape"]:
+        for name in ("C3_tiny", "C4_1.3B", "C5_8B_shape"):
             llm[name] = llm_leg(torch, evk, name, comm, rank, ws)
         extra["llm"] = llm
         if comm:

@@ -71,6 +71,7 @@ SIGNATURES = {
     "evkcu_embed": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _int, _vp],
     "evkcu_greedy_sample": [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _int, _vp],
     "evkcu_greedy_sample_noalloc": [_vp, _vp, _u32, _u32, _u32, _u32, _u32, _u32, _u32, _int, _vp],
+    "evkcu_rms_norm_rope": [_vp, _vp, _vp, _u32, _u32, _u32, _u32, _u32, _f32, _f32, _int, _vp],
     # training side
     "evkcu_relu": [_vp, _vp, _u64, _int, _vp],
     "evkcu_relu_backward": [_vp, _vp, _vp, _u64, _int, _vp],
@@ -244,6 +245,15 @@ def rms_norm(x, out, eps=1e-4, gamma=None, stream=None):
 def rope(x, out, batch, seq_len, dim, base=10000.0, head_dim=0, pos_offset=0, stream=None):
     _check("evkcu_rope", lib().evkcu_rope(_ptr(x), _ptr(out), batch, seq_len, dim, head_dim, pos_offset, base,
                                           _dtype_code(x), _stream(stream)))
+    return out
+
+
+def rms_norm_rope(x, out, seq_len, eps=1e-5, base=10000.0, head_dim=0, pos_offset=0, gamma=None, stream=None):
+    """Fused rms_norm + rope over rows of the last dimension (evkcu_rms_norm_rope)."""
+    D = x.shape[-1]
+    _check("evkcu_rms_norm_rope", lib().evkcu_rms_norm_rope(
+        _ptr(x), _ptr(out), _ptr(gamma), x.numel() // D, seq_len, D, head_dim, pos_offset, eps, base,
+        _dtype_code(x), _stream(stream)))
     return out
 
 
@@ -439,6 +449,8 @@ SIGNATURES.update({
     "evkcu_llm_prefill": [_vp, _vp, _u32, _u32, _vp, _vp, _vp],
     "evkcu_llm_decode": [_vp, _vp, _vp, _vp, _vp],
     "evkcu_llm_length": [_vp],
+    "evkcu_llm_load": [_vp, ctypes.c_char_p, _vp],
+    "evkcu_llm_save": [_vp, ctypes.c_char_p, _vp],
 })
 _RET["evkcu_llm_length"] = ctypes.c_uint32
 
@@ -493,6 +505,14 @@ class Llm:
         _check("evkcu_llm_set_weight", lib().evkcu_llm_set_weight(self.handle, name.encode(), layer, _ptr(tensor),
                                                                   _stream(stream)))
 
+    def load(self, path: str, stream=None):
+        """Loads every weight from a weight blob (see write_weight_blob)."""
+        _check("evkcu_llm_load", lib().evkcu_llm_load(self.handle, os.fsencode(path), _stream(stream)))
+
+    def save(self, path: str, stream=None):
+        """Writes every weight to a weight blob (single-GPU models)."""
+        _check("evkcu_llm_save", lib().evkcu_llm_save(self.handle, os.fsencode(path), _stream(stream)))
+
     def prefill(self, tokens, next_ids, logits=None, stream=None):
         B, S = tokens.shape
         _check("evkcu_llm_prefill", lib().evkcu_llm_prefill(self.handle, _ptr(tokens), B, S, _ptr(next_ids),
@@ -507,3 +527,47 @@ class Llm:
     @property
     def length(self) -> int:
         return int(lib().evkcu_llm_length(self.handle))
+
+
+# ------------------------------------------------------------- weight blob --
+BLOB_MAGIC = b"EVKWBLOB"
+
+
+def blob_layout(layers, d_model, heads, hidden, vocab, kv_heads=None, tied_embeddings=True):
+    """(name, layer, shape) of every tensor of a weight blob, in file order
+    (include/evkcu.h, evkcu_llm_load)."""
+    kv = kv_heads or heads
+    dh = d_model // heads
+    out = [("embedding", 0, (vocab, d_model))]
+    if not tied_embeddings:
+        out.append(("lm_head", 0, (d_model, vocab)))
+    for l in range(layers):
+        out += [("wqkv", l, (d_model, (heads + 2 * kv) * dh)), ("wo", l, (heads * dh, d_model)),
+                ("w1", l, (d_model, hidden)), ("w2", l, (hidden, d_model))]
+    return out
+
+
+def write_weight_blob(path, weights, layers, d_model, heads, hidden, vocab, kv_heads=None, tied_embeddings=True,
+                      dtype=F16):
+    """Writes a weight blob from host arrays of 2-byte storage values.
+
+    weights maps (name, layer) to an array with the blob_layout shape (any
+    2-byte dtype: numpy uint16/float16, or torch half/bfloat16 on the CPU)."""
+    import numpy as np
+
+    kv = kv_heads or heads
+    header = np.zeros(16, np.uint32)
+    header[:2] = np.frombuffer(BLOB_MAGIC, np.uint32)
+    header[2:11] = [1, dtype, layers, d_model, heads, kv, hidden, vocab, 1 if tied_embeddings else 0]
+    with open(path, "wb") as f:
+        f.write(header.tobytes())
+        for name, layer, shape in blob_layout(layers, d_model, heads, hidden, vocab, kv, tied_embeddings):
+            a = weights[(name, layer)]
+            if hasattr(a, "numpy"):
+                import torch
+
+                a = a.detach().contiguous().cpu().view(torch.int16).numpy()
+            a = np.ascontiguousarray(a)
+            if a.dtype.itemsize != 2 or a.size != shape[0] * shape[1]:
+                raise ValueError(f"{name}[{layer}]: expected {shape} of 2-byte values, got {a.shape} {a.dtype}")
+            f.write(a.view(np.uint16).tobytes())

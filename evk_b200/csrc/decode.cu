@@ -392,7 +392,12 @@ int launch_decode(const void* q, const void* k, const void* v, void* o, uint32_t
     }
     // One resident wave: split positions over the CTA slots left per (b, g, head group).
     const uint64_t slots = (uint64_t)per_sm * ds->sm_count;
-    const uint64_t want = std::max<uint64_t>(1, slots / ctas_wo_split);
+    uint64_t want = std::max<uint64_t>(1, slots / ctas_wo_split);
+    static const int forced_splits = [] {
+        const char* e = getenv("EVKCU_DECODE_SPLITS");
+        return e ? atoi(e) : 0;
+    }();
+    if (forced_splits > 0) want = (uint64_t)forced_splits;
     uint32_t chunk = (uint32_t)std::max<uint64_t>(ROWS, (cur_len + want - 1) / want);
     chunk = (chunk + ROWS - 1) / ROWS * ROWS;
     const uint32_t nsplit = (cur_len + chunk - 1) / chunk;

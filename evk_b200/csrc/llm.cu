@@ -20,6 +20,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <string>
 #include <unordered_map>
@@ -567,6 +568,121 @@ extern "C" int evkcu_llm_set_weight(evkcu_llm* m, const char* name, uint32_t lay
     if (n == "w1") return copy2d(L.w1, m->Fl, 0, src, c.hidden, (size_t)rk * m->Fl, m->Fl, D);
     if (n == "w2") return copy2d(L.w2, D, 0, (const char*)src + (size_t)rk * m->Fl * D * kE, D, 0, D, m->Fl);
     return fail(EVKCU_BAD_ARG, "evkcu_llm_set_weight: unknown weight " + n);
+}
+
+// ---- weight blob ------------------------------------------------------------
+// One file holding every weight of a model in its storage type, unsharded:
+// a 64-byte header (magic "EVKWBLOB", then uint32 version 1, dtype, layers,
+// d_model, heads, kv_heads, hidden, vocab, tied_embeddings, zero padding),
+// then the tensors row-major in this order: embedding [V, D], lm_head [D, V]
+// (untied models only), and per layer wqkv [D, (H + 2 Hkv) Dh], wo [H Dh, D],
+// w1 [D, F], w2 [F, D] (the layouts of evkcu_llm_set_weight).
+namespace {
+constexpr char kBlobMagic[8] = {'E', 'V', 'K', 'W', 'B', 'L', 'O', 'B'};
+struct BlobHeader {
+    char magic[8];
+    uint32_t version, dtype, layers, d_model, heads, kv_heads, hidden, vocab, tied;
+    uint32_t pad[5];
+};
+static_assert(sizeof(BlobHeader) == 64, "blob header is 64 bytes");
+
+struct BlobTensor {
+    const char* name;
+    uint32_t layer;
+    uint64_t elems;
+};
+std::vector<BlobTensor> blob_layout(const evkcu_llm_config& c) {
+    const uint64_t D = c.d_model, Dh = D / c.heads, V = c.vocab, F = c.hidden;
+    std::vector<BlobTensor> t;
+    t.push_back({"embedding", 0, V * D});
+    if (!c.tied_embeddings) t.push_back({"lm_head", 0, D * V});
+    for (uint32_t l = 0; l < c.layers; ++l) {
+        t.push_back({"wqkv", l, D * (c.heads + 2ull * c.kv_heads) * Dh});
+        t.push_back({"wo", l, (uint64_t)c.heads * Dh * D});
+        t.push_back({"w1", l, D * F});
+        t.push_back({"w2", l, F * D});
+    }
+    return t;
+}
+}  // namespace
+
+extern "C" int evkcu_llm_load(evkcu_llm* m, const char* path, void* stream) {
+    EVKCU_CHECK_ARG(m && path, EVKCU_BAD_ARG, "evkcu_llm_load: null pointer");
+    const evkcu_llm_config& c = m->cfg;
+    FILE* f = std::fopen(path, "rb");
+    EVKCU_CHECK_ARG(f, EVKCU_BAD_ARG, std::string("evkcu_llm_load: cannot open ") + path);
+    BlobHeader h{};
+    const bool hdr_ok = std::fread(&h, sizeof(h), 1, f) == 1 && std::memcmp(h.magic, kBlobMagic, 8) == 0 &&
+                        h.version == 1;
+    const bool cfg_ok = hdr_ok && h.dtype == (uint32_t)c.dtype && h.layers == c.layers && h.d_model == c.d_model &&
+                        h.heads == c.heads && h.kv_heads == c.kv_heads && h.hidden == c.hidden &&
+                        h.vocab == c.vocab && h.tied == (c.tied_embeddings ? 1u : 0u);
+    if (!cfg_ok) {
+        std::fclose(f);
+        return fail(hdr_ok ? EVKCU_BAD_SHAPE : EVKCU_BAD_ARG,
+                    hdr_ok ? "evkcu_llm_load: blob does not match the model configuration"
+                           : "evkcu_llm_load: not a version-1 weight blob");
+    }
+    cudaStream_t st = as_stream(stream);
+    std::vector<uint16_t> host;
+    for (const BlobTensor& t : blob_layout(c)) {
+        host.resize(t.elems);
+        if (std::fread(host.data(), kE, t.elems, f) != t.elems) {
+            std::fclose(f);
+            return fail(EVKCU_BAD_SHAPE, std::string("evkcu_llm_load: file ends inside ") + t.name);
+        }
+        // set_weight copies this rank's shard straight from host memory.
+        int r = evkcu_llm_set_weight(m, t.name, t.layer, host.data(), stream);
+        if (r == EVKCU_OK && cudaStreamSynchronize(st) != cudaSuccess) r = cuda_fail(cudaGetLastError(), "load sync");
+        if (r != EVKCU_OK) {
+            std::fclose(f);
+            return r;
+        }
+    }
+    std::fclose(f);
+    return EVKCU_OK;
+}
+
+extern "C" int evkcu_llm_save(evkcu_llm* m, const char* path, void* stream) {
+    EVKCU_CHECK_ARG(m && path, EVKCU_BAD_ARG, "evkcu_llm_save: null pointer");
+    const evkcu_llm_config& c = m->cfg;
+    EVKCU_CHECK_ARG(c.tp_size == 1, EVKCU_UNSUPPORTED, "evkcu_llm_save: a tensor-parallel rank holds only shards");
+    cudaStream_t st = as_stream(stream);
+    EVKCU_CUDA_TRY(cudaStreamSynchronize(st));
+    FILE* f = std::fopen(path, "wb");
+    EVKCU_CHECK_ARG(f, EVKCU_BAD_ARG, std::string("evkcu_llm_save: cannot create ") + path);
+    BlobHeader h{};
+    std::memcpy(h.magic, kBlobMagic, 8);
+    h.version = 1;
+    h.dtype = (uint32_t)c.dtype;
+    h.layers = c.layers;
+    h.d_model = c.d_model;
+    h.heads = c.heads;
+    h.kv_heads = c.kv_heads;
+    h.hidden = c.hidden;
+    h.vocab = c.vocab;
+    h.tied = c.tied_embeddings ? 1u : 0u;
+    bool ok = std::fwrite(&h, sizeof(h), 1, f) == 1;
+    std::vector<uint16_t> host;
+    for (const BlobTensor& t : blob_layout(c)) {
+        if (!ok) break;
+        const void* src = nullptr;
+        if (!std::strcmp(t.name, "embedding")) src = m->emb;
+        else if (!std::strcmp(t.name, "lm_head")) src = m->lm_head;
+        else if (!std::strcmp(t.name, "wqkv")) src = m->layers[t.layer].wqkv;
+        else if (!std::strcmp(t.name, "wo")) src = m->layers[t.layer].wo;
+        else if (!std::strcmp(t.name, "w1")) src = m->layers[t.layer].w1;
+        else src = m->layers[t.layer].w2;
+        host.resize(t.elems);
+        if (cudaMemcpy(host.data(), src, t.elems * kE, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            std::fclose(f);
+            return cuda_fail(cudaGetLastError(), "evkcu_llm_save: device read");
+        }
+        ok = std::fwrite(host.data(), kE, t.elems, f) == t.elems;
+    }
+    ok = (std::fclose(f) == 0) && ok;
+    EVKCU_CHECK_ARG(ok, EVKCU_BAD_ARG, std::string("evkcu_llm_save: write failed: ") + path);
+    return EVKCU_OK;
 }
 
 extern "C" int evkcu_llm_prefill(evkcu_llm* m, const uint32_t* tokens, uint32_t B, uint32_t S, uint32_t* next_ids,

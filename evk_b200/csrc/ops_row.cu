@@ -271,6 +271,59 @@ inline unsigned row_threads(uint32_t items) {
     return t;
 }
 
+// --------------------------------------------------------- rms_norm + rope --
+// The two bandwidth ops fused (rows of `dim`): y = rope(rms_norm(x) [* gamma])
+// with rms_norm as above (shaders/rms_norm.comp:21-48) and rope as
+// rope_kernel (shaders/rope.comp:18-40, per head_dim slice, position
+// row % seq_len + pos_offset), without the intermediate rounding to storage:
+// one read and one write per element instead of two of each.
+template <typename T>
+__global__ void rms_norm_rope_kernel(const T* __restrict__ in, T* __restrict__ out, const T* __restrict__ gamma,
+                                     uint32_t D, uint32_t seq_len, uint32_t head_dim, uint32_t pos_offset, float eps,
+                                     float base) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float sh[32];
+    const uint64_t row = blockIdx.x;
+    const Vec8* xv = reinterpret_cast<const Vec8*>(in + row * D);
+    const Vec8* gv = reinterpret_cast<const Vec8*>(gamma);
+    Vec8* yv = reinterpret_cast<Vec8*>(out + row * D);
+    float ss = 0.0f;
+    for (uint32_t c = threadIdx.x; c < D / 8; c += blockDim.x) {
+        float f[8];
+        unpack8<T>(xv[c], f);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float v = fminf(fmaxf(f[k], -65504.0f), 65504.0f);
+            ss += v * v;
+        }
+    }
+    const float inv = rsqrtf(block_sum(ss, sh) / (float)D + eps);
+    const float t = (float)((uint32_t)(row % seq_len) + pos_offset);
+    for (uint32_t c = threadIdx.x; c < D / 8; c += blockDim.x) {
+        float f[8], g[8];
+        unpack8<T>(xv[c], f);
+        if (gamma) unpack8<T>(gv[c], g);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float v = fminf(fmaxf(f[k], -65504.0f), 65504.0f) * inv;
+            f[k] = gamma ? v * g[k] : v;
+        }
+        const uint32_t c0 = c * 8;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t p = ((c0 % head_dim) >> 1) + k;
+            const float inv_freq = powf(base, -2.0f * (float)p / (float)head_dim);
+            float sn, cs;
+            sincosf(t * inv_freq, &sn, &cs);
+            const float x0 = f[2 * k], x1 = f[2 * k + 1];
+            f[2 * k] = x0 * cs - x1 * sn;
+            f[2 * k + 1] = x0 * sn + x1 * cs;
+        }
+        yv[c] = pack8<T>(f);
+    }
+}
+
 }  // namespace
 }  // namespace evkcu
 
@@ -335,5 +388,22 @@ extern "C" int evkcu_rope(const void* in, void* out, uint32_t batch, uint32_t se
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
         return launch_pdl("evkcu_rope", rope_kernel<T>, grid, 256, 0, as_stream(stream), (const T*)in, (T*)out, rows,
                           seq_len, dim, head_dim, pos_offset, base, vec);
+    });
+}
+
+extern "C" int evkcu_rms_norm_rope(const void* in, void* out, const void* gamma, uint32_t rows, uint32_t seq_len,
+                                   uint32_t dim, uint32_t head_dim, uint32_t pos_offset, float eps, float base,
+                                   int dtype, void* stream) {
+    if (rows == 0) return EVKCU_OK;
+    EVKCU_CHECK_ARG(in && out, EVKCU_BAD_ARG, "evkcu_rms_norm_rope: null pointer");
+    if (head_dim == 0) head_dim = dim;
+    EVKCU_CHECK_ARG(seq_len > 0 && dim > 0 && dim % 8 == 0 && head_dim % 8 == 0 && dim % head_dim == 0,
+                    EVKCU_BAD_SHAPE, "evkcu_rms_norm_rope: dim and head_dim must be multiples of 8, head_dim | dim");
+    EVKCU_CHECK_ARG(aligned16(in) && aligned16(out) && (!gamma || aligned16(gamma)), EVKCU_BAD_ALIGN,
+                    "evkcu_rms_norm_rope: buffers must be 16-byte aligned");
+    const unsigned threads = row_threads(dim / 8);
+    return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
+        return launch_pdl("evkcu_rms_norm_rope", rms_norm_rope_kernel<T>, rows, threads, 0, as_stream(stream),
+                          (const T*)in, (T*)out, (const T*)gamma, dim, seq_len, head_dim, pos_offset, eps, base);
     });
 }

@@ -193,6 +193,15 @@ int evkcu_single_query_attention_devlen(const void* q, const void* kcache, const
                                         uint32_t max_len, const uint32_t* d_cur_len, float scale,
                                         int dtype, void* stream);
 
+/* Fused RMSNorm + RoPE (extension: the two bandwidth ops of evk_ai.h:607-610
+ * and 587-591 in one pass).  rows = batch * seq_len rows of `dim`:
+ * out = rope(rms_norm(in, eps) [* gamma]) with RoPE over each head_dim slice
+ * (0 = the whole row, as the reference) at positions row % seq_len +
+ * pos_offset; no rounding between the two.  dim, head_dim multiples of 8;
+ * 16-byte-aligned buffers.                                                  */
+int evkcu_rms_norm_rope(const void* in, void* out, const void* gamma, uint32_t rows, uint32_t seq_len, uint32_t dim,
+                        uint32_t head_dim, uint32_t pos_offset, float eps, float base, int dtype, void* stream);
+
 /* ---- training side ---------------------------------------------------------
  * The reference's training operators (evk_ai.h:474-615).  Backward passes
  * accumulate into their gradient tensor (grad_in += ...) as the shaders do;
@@ -314,6 +323,17 @@ int evkcu_llm_init_random(evkcu_llm* m, uint64_t seed, float std, void* stream);
  * [D, (H + 2 Hkv) Dh] (columns: q heads, k heads, v heads), "wo" [H Dh, D],
  * "w1" [D, F], "w2" [F, D].                                                  */
 int evkcu_llm_set_weight(evkcu_llm* m, const char* name, uint32_t layer, const void* src, void* stream);
+/* Weight blob (extension; the reference keeps only an in-memory parameter
+ * snapshot, example/main_llm.cpp:306-354): one file with every weight of the
+ * model in its storage type, unsharded.  Layout: a 64-byte header (magic
+ * "EVKWBLOB", uint32 version = 1, dtype, layers, d_model, heads, kv_heads,
+ * hidden, vocab, tied_embeddings, zero padding), then row-major tensors in
+ * the order embedding, lm_head (untied only), and per layer wqkv, wo, w1,
+ * w2, each in the layout of evkcu_llm_set_weight.  load checks the header
+ * against the model's configuration and keeps this rank's shards; save
+ * needs tp_size == 1.  Both synchronise the stream.                        */
+int evkcu_llm_load(evkcu_llm* m, const char* path, void* stream);
+int evkcu_llm_save(evkcu_llm* m, const char* path, void* stream);
 /* Prefill: tokens [B, S] (uint32, device) -> KV cache positions 0..S-1 and
  * the next token per sequence (next_ids [B], uint32, device).  Resets the
  * cache.  Optionally logits_out [B, vocab] (device, storage dtype) receives

@@ -220,3 +220,23 @@ def test_greedy_sample_signed_zero_max(dtype, V):
     oracle.greedy_sample(l, ref, B, 1, V, 0, 0, V, dc)
     assert np.array_equal(out.cpu().numpy().view(np.uint32), ref), (out, ref)
     assert ref[0] == 3
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("B,S,D,hd,off,gamma", [(1, 128, 512, 0, 0, False), (2, 17, 256, 64, 5, True),
+                                                (8, 1, 2048, 128, 300, True), (4, 64, 4096, 128, 0, False)])
+def test_rms_norm_rope_fused_vs_oracle(dtype, B, S, D, hd, off, gamma):
+    """evkcu_rms_norm_rope against the oracle's rms_norm then rope (which
+    rounds in between: one storage ulp of slack in the tolerance)."""
+    dc = dcode(dtype)
+    rows = B * S
+    x = oracle.normal(rows * D, 60, 3.0, dtype=dc)
+    g = oracle.normal(D, 61, dtype=dc) if gamma else None
+    out = torch.empty(rows, D, dtype=dtype, device="cuda")
+    ev().rms_norm_rope(dev(x, dtype).view(rows, D), out, S, 1e-5, 10000.0, hd, off,
+                       gamma=dev(g, dtype) if gamma else None)
+    n = np.empty_like(x)
+    oracle.rms_norm(x, n, rows, D, 1e-5, gamma=g, dtype=dc)
+    r = np.empty_like(x)
+    oracle.rope(n, r, B, S, D, hd, off, 10000.0, dc)
+    assert_close(u16(out).ravel(), r, dc, rel_l2=1e-3 if dc == 0 else 4e-3, ulps=2.0, what="rms_norm_rope")
