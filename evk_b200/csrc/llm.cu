@@ -28,6 +28,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "decode_mega.cuh"
 #include "greedy_key.cuh"
 
 namespace evkcu {
@@ -155,6 +156,10 @@ struct evkcu_llm {
     bool ar_ready = false;
     std::vector<void*> ipc_opened;
     uint32_t *gin = nullptr, *gout = nullptr;  // fixed ids in/out words of the decode graph
+    // Persistent one-kernel decode step (decode_mega.cu) for small models.
+    void* mega_scratch = nullptr;
+    void* mega_layers = nullptr;  // device MegaLayer [layers]
+    bool mega_ok = false;
     uint32_t cur_len = 0, batch = 0;
     std::vector<void*> allocs;
     std::unordered_map<uint32_t, cudaGraphExec_t> graphs;  // by batch size
@@ -301,9 +306,41 @@ int head_and_sample(evkcu_llm* m, const void* xrows, uint32_t B, uint32_t* next_
     return EVKCU_OK;
 }
 
+bool use_decode_mega(const evkcu_llm* m) { return m->mega_ok; }
+
 int decode_body(evkcu_llm* m, const uint32_t* ids, uint32_t* next_ids, void* logits_out, cudaStream_t st) {
     const evkcu_llm_config& c = m->cfg;
     const uint32_t B = m->batch;
+    if (use_decode_mega(m)) {
+        MegaHost h{};
+        h.B = B;
+        h.D = c.d_model;
+        h.H = c.heads;
+        h.Hkv = c.kv_heads;
+        h.Dh = m->Dh;
+        h.F = c.hidden;
+        h.V = c.vocab;
+        h.layers = c.layers;
+        h.max_seq = c.max_seq;
+        h.tied = c.tied_embeddings ? 1u : 0u;
+        h.eps = c.eps;
+        h.rope_base = c.rope_base;
+        h.emb = m->emb;
+        h.lm_head = m->lm_head;
+        h.layer_table = m->mega_layers;
+        h.x = m->x;
+        h.q = m->q;
+        h.attn = m->attn;
+        h.h1 = m->h1;
+        h.logits = logits_out;
+        h.rope_cs = m->rope_cs;
+        h.d_pos = m->d_pos;
+        h.d_len = m->d_len;
+        h.ids_in = ids;
+        h.ids_out = next_ids;
+        h.scratch = m->mega_scratch;
+        return decode_mega_step(h, c.dtype, st);
+    }
     LLM_TRY(evkcu_embed(m->emb, ids, m->x, c.vocab, c.d_model, B, 4, c.dtype, st));
     LLM_TRY(run_blocks(m, B, 1, true, st));
     LLM_TRY(head_and_sample(m, m->x, B, next_ids, logits_out, st));
@@ -485,6 +522,30 @@ extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_l
     if ((r = rope_table(m->rope_cs, c.max_seq, Dh, c.rope_base, 0)) != EVKCU_OK) {
         evkcu_llm_destroy(m);
         return r;
+    }
+    // Opt-in (EVKCU_DECODE_MEGA=1 when the model is created): measured slower
+    // than the per-op chain at C3 (0.28 vs 0.20 ms per step: a grid barrier
+    // costs 2.3 us and each phase adds L2 round trips).
+    const char* mega_env = getenv("EVKCU_DECODE_MEGA");
+    if (t == 1 && mega_env && atoi(mega_env) == 1 &&
+        decode_mega_supported(c.max_batch, c.d_model, c.heads, c.kv_heads, Dh, c.hidden, c.vocab,
+                              c.tied_embeddings != 0)) {
+        // The persistent decode step: its scratch (zero-filled) and the
+        // per-layer pointer table it reads.
+        const size_t sb = decode_mega_scratch_bytes(c.max_batch, c.d_model, c.heads, c.kv_heads, Dh, c.hidden,
+                                                    c.max_seq, ds->sm_count);
+        std::vector<MegaLayer> tab(c.layers);
+        for (uint32_t l = 0; l < c.layers; ++l)
+            tab[l] = {m->layers[l].wqkv, m->layers[l].wo, m->layers[l].w1, m->layers[l].w2, m->layers[l].kc,
+                      m->layers[l].vc};
+        if ((r = llm_alloc(m, &m->mega_scratch, sb)) != EVKCU_OK ||
+            (r = llm_alloc(m, &m->mega_layers, sizeof(MegaLayer) * c.layers)) != EVKCU_OK) {
+            evkcu_llm_destroy(m);
+            return r;
+        }
+        EVKCU_CUDA_TRY(cudaMemset(m->mega_scratch, 0, sb));
+        EVKCU_CUDA_TRY(cudaMemcpy(m->mega_layers, tab.data(), sizeof(MegaLayer) * c.layers, cudaMemcpyHostToDevice));
+        m->mega_ok = true;
     }
     EVKCU_CUDA_TRY(cudaDeviceSynchronize());
     if (t > 1) setup_allreduce(m, xch);  // all ranks fall back to NCCL unless every rank mapped its peers

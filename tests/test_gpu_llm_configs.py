@@ -47,3 +47,25 @@ def test_llm_config_greedy_vs_oracle(name):
         m.close()
     assert stats["checked"] == B * (steps + 1)
     evk_b200.check_device_error()
+
+
+def test_c3_persistent_decode_step_vs_oracle(monkeypatch):
+    """The persistent one-kernel decode step (opt-in, EVKCU_DECODE_MEGA=1 at
+    model creation) on the C3 model: same protocol as above (32 steps)."""
+    import evk_b200
+
+    monkeypatch.setenv("EVKCU_DECODE_MEGA", "1")
+    L, D, H, F, V, tied, dt, B, S, _ = CONFIGS["C3"]
+    steps = 32
+    evk_b200.init(0)
+    ref = RefModel(L, D, H, F, V, tied, dtype=dt, seed=42)
+    max_len = S + steps + 1
+    m = evk_b200.Llm(L, D, H, F, V, B, max_len, dtype=dt, tied_embeddings=tied)
+    try:
+        load_weights(m, ref, torch.float16)
+        prompt = oracle.uniform_ids(B * S, 7, 0, V, 4).astype(np.int64).reshape(B, S)
+        stats = teacher_forced_parity(ref, m, prompt, steps, dt, torch.float16, max_len, "C3 persistent step")
+    finally:
+        m.close()
+    assert stats["checked"] == B * (steps + 1)
+    evk_b200.check_device_error()
