@@ -40,10 +40,15 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when th
 //             sub-partition, so one tile's exponentials overlap the others'
 //             row max, P store and barrier waits.
 //   Dh = 128: two tiles over 128-key blocks.
-template <int DH, int NT, int FN_, int POLY_ = 0, bool QT_ = false>
+template <int DH, int NT, int FN_, int POLY_ = 0, bool QT_ = false, int CH_ = 1>
 struct FlashCfg {
     static constexpr int FN = FN_;    // keys per block
     static constexpr int POLY = POLY_;
+    // Column halves: with CH = 2 each tile's softmax is two warpgroups, one
+    // per half of the S (and O) columns, so four softmax warps share each SM
+    // sub-partition; the halves exchange row maxima (and, at the end, row
+    // sums) through shared memory under a 64-thread named barrier.
+    static constexpr int CH = CH_;
     // Q in TMEM: the softmax warps store their Q rows into TMEM once per
     // item and the S MMA reads its A operand from there (A from shared
     // memory costs a 128 x 16 operand fetch per MMA: 102 vs 73 clocks for
@@ -65,17 +70,35 @@ struct FlashCfg {
     static constexpr int OFF_K = OFF_Q + (QT ? 0 : NT * Q_BYTES);
     static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
     static constexpr int OFF_BAR = OFF_V + STAGES * KV_BYTES;
-    static constexpr int BAR_BYTES = ((2 + 3 * STAGES + 6 * NT) * 8 + 16 + 127) / 128 * 128;
-    static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024;
-    static constexpr int THREADS = 128 + NT * 128;
+    static constexpr int BAR_BYTES = ((2 + 3 * STAGES + 10 * NT) * 8 + 16 + 127) / 128 * 128;
+    static constexpr int OFF_X = OFF_BAR + BAR_BYTES;  // CH = 2: row max / sum exchange
+    static constexpr int X_BYTES = CH == 2 ? (2 + 1) * NT * CH * FM * 4 : 0;
+    static constexpr int SMEM = OFF_X + X_BYTES + 1024;
+    static constexpr int THREADS = 128 + NT * CH * 128;
     static __device__ __forceinline__ uint32_t col_s(int t) { return t * TSTRIDE; }
     static __device__ __forceinline__ uint32_t col_o(int t) { return t * TSTRIDE + FN; }
     static __device__ __forceinline__ uint32_t col_p(int t) { return ALIAS_P ? t * TSTRIDE : t * TSTRIDE + FN + DH; }
     static __device__ __forceinline__ uint32_t col_q(int t) { return t * TSTRIDE + FN + DH; }
 };
 static_assert(FlashCfg<64, 2, 128>::SMEM <= 227 * 1024 && FlashCfg<128, 2, 128>::SMEM <= 227 * 1024 &&
-                  FlashCfg<64, 4, 64>::SMEM <= 227 * 1024 && FlashCfg<64, 2, 128, 0, true>::SMEM <= 227 * 1024,
+                  FlashCfg<64, 4, 64>::SMEM <= 227 * 1024 && FlashCfg<64, 2, 128, 0, true>::SMEM <= 227 * 1024 &&
+                  FlashCfg<64, 2, 128, 0, false, 2>::SMEM <= 227 * 1024,
               "flash smem");
+
+// Phase trace (build with -DEVK_FLASH_TRACE only): clock64 stamps of CTA 0's
+// first item, read back with evkcu_debug_flash_trace.  Slots 0 / 1: softmax
+// tile 0 / 1 (row group 0), 2: S issuer, 3: PV issuer; [block][event].
+#ifdef EVK_FLASH_TRACE
+__device__ unsigned long long g_ftrace[4][64][8];
+#define FTRACE(slot, blk, ev)                                                              \
+    do {                                                                                   \
+        if (blockIdx.x == 0 && (threadIdx.x & 31) == 0 && (blk) < 64) g_ftrace[slot][blk][ev] = clock64(); \
+    } while (0)
+#else
+#define FTRACE(slot, blk, ev) \
+    do {                      \
+    } while (0)
+#endif
 
 // max(a, b, c) in one instruction (sm_100).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -186,7 +209,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     uint64_t* pv_done = p_full + NT;    // [NT]
     uint64_t* o_free = pv_done + NT;    // [NT]
     uint64_t* q_tm = o_free + NT;       // [NT] Q_t stored in TMEM (Cfg::QT)
-    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(q_tm + NT);
+    uint64_t* x_bar = q_tm + NT;        // [NT * 4] column-half pairs exchanged a value (Cfg::CH = 2)
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(x_bar + 4 * NT);
     volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -225,11 +249,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         }
         for (int t = 0; t < NT; ++t) {
             mbar_init(&s_full[t], 1);
-            mbar_init(&s_free[t], 4);
-            mbar_init(&p_full[t], 4);
+            mbar_init(&s_free[t], 4 * Cfg::CH);
+            mbar_init(&p_full[t], 4 * Cfg::CH);
             mbar_init(&pv_done[t], 1);
-            mbar_init(&o_free[t], 4);
-            mbar_init(&q_tm[t], 4);
+            mbar_init(&o_free[t], 4 * Cfg::CH);
+            mbar_init(&q_tm[t], 4 * Cfg::CH);
+            for (int qq = 0; qq < 4; ++qq) mbar_init(&x_bar[4 * t + qq], 2);
         }
         *s_abort = 0;
         fence_barrier_init();
@@ -249,7 +274,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     // warpgroup (producer, issuers) hands registers to the softmax
     // warpgroups: 128 * 64 + 512 * 104 = 61,440 = 640 * 96.
     if (warp < 4) {
-    if constexpr (NT == 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 64;\n" ::: "memory");
+    if constexpr (Cfg::THREADS == 640) asm volatile("setmaxnreg.dec.sync.aligned.u32 64;\n" ::: "memory");
     if (warp == 0) {
         // ------------------------------------------------ TMA producer ----
         if (lane == 0) {
@@ -342,6 +367,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                         // S_t(j) overwrites S_t(j - 1): softmax t must have
                         // read it, and with P aliased into S, PV_t(j - 1)
                         // must have read P (which also implies the former).
+                        if (it == 0) FTRACE(2, j, 2 * t);
                         ok = gj == 0 || probe(lane == 0 && mbar_wait(&s_reuse[t], (gj - 1) & 1, s_abort, err,
                                                                      kTimeoutFlash));
                         // Q in TMEM: the first S of an item waits until
@@ -366,6 +392,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                             mma_commit(&s_full[t]);
                         }
                         __syncwarp();
+                        if (it == 0) FTRACE(2, j, 2 * t + 1);
                     }
                     if (!ok) break;
                     // Q is free once every S of this item has completed.
@@ -377,6 +404,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                     for (int t = 0; t < NT; ++t) {
                         const uint32_t gj = gs[t] + j;
                         if (!ok || j >= nblk[t]) continue;
+                        if (it == 0) FTRACE(3, j, 2 * t);
                         ok = probe(lane == 0 && mbar_wait(&p_full[t], gj & 1, s_abort, err, kTimeoutFlash) &&
                                    (j != 0 || ep[t] == 0 ||
                                     mbar_wait(&o_free[t], (ep[t] - 1) & 1, s_abort, err, kTimeoutFlash)));
@@ -393,6 +421,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                             mma_commit(&pv_done[t]);
                         }
                         __syncwarp();
+                        if (it == 0) FTRACE(3, j, 2 * t + 1);
                     }
                     if (!ok) break;
                 }
@@ -410,15 +439,32 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         }
     }
     } else {
-        if constexpr (NT == 4) asm volatile("setmaxnreg.inc.sync.aligned.u32 104;\n" ::: "memory");
+        if constexpr (Cfg::THREADS == 640) asm volatile("setmaxnreg.inc.sync.aligned.u32 104;\n" ::: "memory");
         // --------------------------------------------- softmax warps ----
-        const int t = (warp >> 2) - 1;
+        constexpr int CH = Cfg::CH;
+        constexpr int SC = FN / CH;  // S columns of this warp
+        constexpr int OC = DH / CH;  // O columns of this warp
+        const int sidx = warp - 4;
+        const int t = sidx / (4 * CH);
+        const int half = (sidx / 4) % CH;
         const int quarter = warp & 3;
         const uint32_t row = quarter * 32 + lane;  // TMEM lane == query row in the tile
         const uint32_t lane_addr = tmem + ((uint32_t)(quarter * 32) << 16);
-        const uint32_t s_addr = lane_addr + Cfg::col_s(t);
-        const uint32_t o_addr = lane_addr + Cfg::col_o(t);
-        const uint32_t p_addr = lane_addr + Cfg::col_p(t);
+        const uint32_t s_addr = lane_addr + Cfg::col_s(t) + half * SC;
+        const uint32_t o_addr = lane_addr + Cfg::col_o(t) + half * OC;
+        const uint32_t p_addr = lane_addr + Cfg::col_p(t) + half * (SC / 2);
+        // CH = 2: exchange slots [parity][t][half][row] for maxima, then
+        // [t][half][row] for the final row sums; the two warps of a row group
+        // meet at mbarrier x_bar[4 t + quarter] (one arrival per warp, bounded
+        // wait), xph counting its completed phases.
+        float* xch = reinterpret_cast<float*>(smem + Cfg::OFF_X);
+        uint64_t* const pair_bar = &x_bar[4 * t + quarter];
+        uint32_t xph = 0;
+        auto pair_sync = [&]() -> bool {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pair_bar);
+            return mbar_wait(pair_bar, (xph++) & 1, s_abort, err, kTimeoutFlash);
+        };
         uint32_t gbase = 0;  // blocks this tile processed in earlier items
         bool ok = true;
         for (uint32_t rd = 0; ok && rd * gridDim.x < items; ++rd) {
@@ -458,39 +504,55 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             float m_ref = -INFINITY, l = 0.0f;
             for (uint32_t j = 0; j < nb; ++j) {
                 const uint32_t gj = gbase + j;
+                const bool trace = gbase == 0 && quarter == 0 && half == 0;
+                if (trace) FTRACE(t, j, 0);
                 if (!mbar_wait(&s_full[t], gj & 1, s_abort, err, kTimeoutFlash)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                uint32_t sr[FN / 32][32];
-#pragma unroll
-                for (int c = 0; c < FN / 32; ++c) tmem_ld32(s_addr + c * 32, sr[c]);
-                tmem_wait_ld();
-                // S is in registers: the tensor core may overwrite it with S_t(j+1).
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&s_free[t]);
-
-                const uint32_t k0 = j * FN;
-                const bool need_mask = (k0 + FN > N) || (causal && k0 + FN > q0[t] + 1);
+                uint32_t sr[SC / 32][32];
+                const uint32_t k0 = j * FN + half * SC;  // first key of this warp's columns
+                const bool need_mask = (k0 + SC > N) || (causal && k0 + SC > q0[t] + 1);
                 // Row max: three-input max, four independent accumulators.
                 float mxa[4];
 #pragma unroll
                 for (int i = 0; i < 4; ++i) mxa[i] = -INFINITY;
-                if (need_mask) {
+                {
 #pragma unroll
-                    for (int c = 0; c < FN / 32; ++c)
+                    for (int c = 0; c < SC / 32; ++c) tmem_ld32(s_addr + c * 32, sr[c]);
+                    tmem_wait_ld();
+                    // S is in registers: the tensor core may overwrite it with S_t(j+1).
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&s_free[t]);
+                    if (trace) FTRACE(t, j, 2);
+                    if (need_mask) {
 #pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (k0 + c * 32 + e >= kmax) sr[c][e] = __float_as_uint(-INFINITY);
+                        for (int c = 0; c < SC / 32; ++c)
+#pragma unroll
+                            for (int e = 0; e < 32; ++e)
+                                if (k0 + c * 32 + e >= kmax) sr[c][e] = __float_as_uint(-INFINITY);
+                    }
+#pragma unroll
+                    for (int c = 0; c < SC / 32; ++c)
+#pragma unroll
+                        for (int e = 0; e < 32; e += 2)
+                            mxa[(e >> 1) & 3] =
+                                fmax3(mxa[(e >> 1) & 3], __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
                 }
-#pragma unroll
-                for (int c = 0; c < FN / 32; ++c)
-#pragma unroll
-                    for (int e = 0; e < 32; e += 2)
-                        mxa[(e >> 1) & 3] = fmax3(mxa[(e >> 1) & 3], __uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-                const float mx = fmax3(fmaxf(mxa[0], mxa[1]), mxa[2], mxa[3]);
+                float mx = fmax3(fmaxf(mxa[0], mxa[1]), mxa[2], mxa[3]);
+                if (trace) FTRACE(t, j, 3);
+                if constexpr (CH == 2) {
+                    // The other half's row maximum (same row, other columns).
+                    float* slot = xch + (((gj & 1) * NT + t) * CH) * FM;
+                    slot[half * FM + row] = mx;
+                    if (!pair_sync()) {
+                        ok = false;
+                        break;
+                    }
+                    mx = fmaxf(mx, slot[(1 - half) * FM + row]);
+                }
                 const float m_cand = fmaxf(m_ref, mx * scale_log2);
                 // Lazy rescale: keep the reference max unless it grew by > 2^8.
                 const bool need = j > 0 && m_cand > m_ref + kRescaleThreshold;
@@ -507,7 +569,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) rs2[i] = make_float2(0.0f, 0.0f);
 #pragma unroll
-                for (int c = 0; c < FN / 32; ++c) {
+                for (int c = 0; c < SC / 32; ++c) {
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
                         float f[8];
@@ -540,6 +602,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                         tmem_st16(p_addr + c * 16, pw);
                     }
                 }
+                if (trace) FTRACE(t, j, 4);
                 if (!kEarlyP && j > 0) {
                     // PV_t(j-1) must be complete before the P columns are
                     // overwritten and before O is rescaled.
@@ -549,6 +612,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                     }
                     tc_fence_after();
                 }
+                if (trace) FTRACE(t, j, 5);
                 const float rs = ((rs2[0].x + rs2[0].y) + (rs2[1].x + rs2[1].y)) +
                                  ((rs2[2].x + rs2[2].y) + (rs2[3].x + rs2[3].y));
                 l = l * alpha + rs;
@@ -557,7 +621,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                     // S_t(j) when P is stored early over S.)
                     constexpr int RC = kEarlyP ? 16 : 32;  // columns per TMEM round trip
 #pragma unroll
-                    for (int c = 0; c < DH / RC; ++c) {
+                    for (int c = 0; c < OC / RC; ++c) {
                         uint32_t rr[RC];
                         if constexpr (RC == 16) tmem_ld16(o_addr + c * RC, rr); else tmem_ld32(o_addr + c * RC, rr);
                         tmem_wait_ld();
@@ -568,7 +632,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                 }
                 if constexpr (!kEarlyP) {
 #pragma unroll
-                    for (int c = 0; c < FN / 32; ++c) {
+                    for (int c = 0; c < SC / 32; ++c) {
                         uint32_t pw[16];
 #pragma unroll
                         for (int i = 0; i < 16; ++i) pw[i] = sr[c][i];
@@ -581,16 +645,24 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[t]);
+                if (trace) FTRACE(t, j, 6);
             }
             if (!ok) break;
             // Epilogue: O / l from TMEM to global memory, then O_t is free.
             const uint32_t glast = gbase + nb - 1;
             if (!mbar_wait(&pv_done[t], glast & 1, s_abort, err, kTimeoutFlash)) break;
             tc_fence_after();
+            if constexpr (CH == 2) {
+                // total row sum = both halves'
+                float* slot = xch + (2 * NT * CH + t * CH) * FM;
+                slot[half * FM + row] = l;
+                if (!pair_sync()) break;
+                l += slot[(1 - half) * FM + row];
+            }
             const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-            T* orow = O + ((uint64_t)b * N + qidx) * ((uint64_t)H * DH) + (uint64_t)h * DH;
+            T* orow = O + ((uint64_t)b * N + qidx) * ((uint64_t)H * DH) + (uint64_t)h * DH + half * OC;
 #pragma unroll
-            for (int c = 0; c < DH / 32; ++c) {
+            for (int c = 0; c < OC / 32; ++c) {
                 uint32_t rr[32];
                 tmem_ld32(o_addr + c * 32, rr);
                 tmem_wait_ld();
@@ -672,10 +744,10 @@ __global__ void __launch_bounds__(256) flash_simt_kernel(const T* __restrict__ Q
     }
 }
 
-template <typename T, int DH, int NT, int FN, int POLY, bool QT = false>
+template <typename T, int DH, int NT, int FN, int POLY, bool QT = false, int CH = 1>
 int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N, uint32_t H,
                     uint32_t Hkv, float scale_log2, int causal, int dtype, uint64_t kv_bstride, cudaStream_t st) {
-    using Cfg = FlashCfg<DH, NT, FN, POLY, QT>;
+    using Cfg = FlashCfg<DH, NT, FN, POLY, QT, CH>;
     CUtensorMap mQ, mK, mV;
     int r;
     if ((r = make_tmap_3d(&mQ, q, (uint64_t)H * DH, N, B, (uint64_t)H * DH, (uint64_t)N * H * DH, 64, FM, dtype))) return r;
@@ -687,7 +759,7 @@ int launch_flash_tc(const void* q, const void* k, const void* v, void* o, uint32
     static bool attr = false;
     if (!attr) {
         EVKCU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
-        if (NT == 4) {
+        if (Cfg::THREADS == 640) {
             // The setmaxnreg split (64 registers for the control warpgroup,
             // 104 for the four softmax warpgroups) must fit the registers the
             // block is launched with, or the increase would wait forever.
@@ -768,6 +840,12 @@ int flash_attention_kv_strided(const void* q, const void* k, const void* v, void
                     case 5:
                         return launch_flash_tc<T, 64, 2, 128, 2, true>(q, k, v, o, B, N, H, Hkv, scale_log2, causal,
                                                                        dtype, kv_bstride, st);
+                    case 6:
+                        return launch_flash_tc<T, 64, 2, 128, 0, false, 2>(q, k, v, o, B, N, H, Hkv, scale_log2,
+                                                                           causal, dtype, kv_bstride, st);
+                    case 7:
+                        return launch_flash_tc<T, 64, 2, 128, 2, false, 2>(q, k, v, o, B, N, H, Hkv, scale_log2,
+                                                                           causal, dtype, kv_bstride, st);
                     default:
                         return launch_flash_tc<T, 64, 2, 128, 0>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype,
                                                                  kv_bstride, st);
@@ -787,6 +865,12 @@ int flash_attention_kv_strided(const void* q, const void* k, const void* v, void
 }
 
 }  // namespace evkcu
+
+#ifdef EVK_FLASH_TRACE
+extern "C" int evkcu_debug_flash_trace(void* host) {
+    return (int)cudaMemcpyFromSymbol(host, evkcu::g_ftrace, sizeof(evkcu::g_ftrace));
+}
+#endif
 
 extern "C" int evkcu_flash_attention(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N,
                                      uint32_t H, uint32_t Hkv, uint32_t Dh, float scale, uint32_t flags, int dtype,
