@@ -449,10 +449,12 @@ SIGNATURES.update({
     "evkcu_llm_prefill": [_vp, _vp, _u32, _u32, _vp, _vp, _vp],
     "evkcu_llm_decode": [_vp, _vp, _vp, _vp, _vp],
     "evkcu_llm_length": [_vp],
+    "evkcu_llm_fused_allreduce": [_vp],
     "evkcu_llm_load": [_vp, ctypes.c_char_p, _vp],
     "evkcu_llm_save": [_vp, ctypes.c_char_p, _vp],
 })
 _RET["evkcu_llm_length"] = ctypes.c_uint32
+_RET["evkcu_llm_fused_allreduce"] = ctypes.c_uint32
 
 
 class Comm:
@@ -523,6 +525,11 @@ class Llm:
         _check("evkcu_llm_decode", lib().evkcu_llm_decode(self.handle, _ptr(ids), _ptr(next_ids), _ptr(logits),
                                                           _stream(stream)))
         return next_ids
+
+    @property
+    def fused_allreduce(self) -> bool:
+        """Whether decode all-reduces run fused over peer memory (tensor parallel)."""
+        return bool(lib().evkcu_llm_fused_allreduce(self.handle))
 
     @property
     def length(self) -> int:

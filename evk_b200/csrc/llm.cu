@@ -565,6 +565,8 @@ extern "C" int evkcu_llm_destroy(evkcu_llm* m) {
 
 extern "C" uint32_t evkcu_llm_length(const evkcu_llm* m) { return m ? m->cur_len : 0; }
 
+extern "C" uint32_t evkcu_llm_fused_allreduce(const evkcu_llm* m) { return m && m->ar_ready ? 1u : 0u; }
+
 extern "C" int evkcu_llm_init_random(evkcu_llm* m, uint64_t seed, float std, void* stream) {
     EVKCU_CHECK_ARG(m, EVKCU_BAD_ARG, "evkcu_llm_init_random: null model");
     const evkcu_llm_config& c = m->cfg;

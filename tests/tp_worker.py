@@ -54,6 +54,29 @@ def main():
         assert np.array_equal(ids_f, ids_l), (ids_f, ids_l)
         if rank == 0:
             oracle_check(ref, prompt, ids_f, logits, 1, MAX_SEQ, f"tp={world} tied={tied}")
+    # The ranks agree on the decode all-reduce path: switching the fused one
+    # off on one rank only makes every rank use NCCL (and decode runs to the
+    # end instead of one rank waiting for peers that never arrive).
+    ref = RefModel(CFG["layers"], CFG["d_model"], CFG["heads"], CFG["hidden"], CFG["vocab"], True, dtype=1, seed=77)
+    paths = {}
+    for one_off in (False, True):
+        if one_off and rank == world - 1:
+            os.environ["EVKCU_DISABLE_FUSED_ALLREDUCE"] = "1"
+        tp = ev.Llm(**CFG, max_batch=B, max_seq=MAX_SEQ, dtype=ev.BF16, tied_embeddings=True, tp_rank=rank,
+                    tp_size=world, comm=comm)
+        os.environ.pop("EVKCU_DISABLE_FUSED_ALLREDUCE", None)
+        load_weights(tp, ref, tdt)
+        ids, _ = gpu_run(tp, prompt, 3, CFG["vocab"], tdt, with_logits=False)
+        ev.check_device_error()
+        flags = [None] * world
+        dist.all_gather_object(flags, (tp.fused_allreduce, ids.tolist()))
+        tp.close()
+        assert all(f == flags[0] for f in flags), flags
+        paths[one_off] = flags[0]
+    assert paths[True][0] is False, "one rank without the fused path: all ranks use NCCL"
+    if rank == 0:
+        print(f"fused all-reduce: on everywhere -> {paths[False][0]}, off on one rank -> {paths[True][0]}",
+              flush=True)
     dist.barrier()
     comm.close()
     dist.destroy_process_group()
