@@ -257,12 +257,23 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
                 go = got;
             }
             const uint32_t rr = q * 32 + lane;  // row within the tile
+            // Fused QKV: this row's position and its (cos, sin) table row,
+            // once per tile (with Dh % 32 == 0 a 32-column chunk never
+            // crosses a head; other head sizes take qkv_rotate per pair).
+            const uint32_t qk_cols = (qr.Hq + qr.Hk) * qr.Dh;
+            const uint32_t rpos = tma_c == 2 ? pos_base + (m0 + rr) % qr.S : 0u;
+            const float2* rtab = (tma_c == 2 && qr.cs && rpos < qr.cs_len && qr.Dh % 32 == 0)
+                                     ? qr.cs + (uint64_t)rpos * (qr.Dh >> 1)
+                                     : nullptr;
 #pragma unroll 1
             for (int c = 0; go && c < BN / 32; ++c) {
                 uint32_t r[32];
                 tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, r);
                 tmem_wait_ld();
                 uint8_t* box = stg + (c >> 1) * (BM * 128) + rr * 128;
+                const uint32_t col0 = n0 + c * 32;
+                const bool rot = tma_c == 2 && col0 < qk_cols;
+                const uint32_t pb = rot ? (col0 % qr.Dh) >> 1 : 0u;  // first rotation pair of the chunk
 #pragma unroll
                 for (int g = 0; g < 4; ++g) {
                     const uint32_t kc = (uint32_t)((c & 1) * 4 + g);
@@ -270,12 +281,23 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
                     float f[8];
 #pragma unroll
                     for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[g * 8 + e]);
-                    if (tma_c == 2) {
-                        const uint32_t col = n0 + c * 32 + g * 8;
-                        if (col < (qr.Hq + qr.Hk) * qr.Dh) {
+                    if (rot) {
+                        if (rtab) {
+                            // pairs pb + 4 g .. pb + 4 g + 3: two 16-byte loads
+                            const float4 t0 = __ldg(reinterpret_cast<const float4*>(rtab + pb + 4 * g));
+                            const float4 t1 = __ldg(reinterpret_cast<const float4*>(rtab + pb + 4 * g + 2));
+                            const float cs4[4] = {t0.x, t0.z, t1.x, t1.z}, sn4[4] = {t0.y, t0.w, t1.y, t1.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float a = f[2 * e] * cs4[e] - f[2 * e + 1] * sn4[e];
+                                const float b = f[2 * e] * sn4[e] + f[2 * e + 1] * cs4[e];
+                                f[2 * e] = a;
+                                f[2 * e + 1] = b;
+                            }
+                        } else {
 #pragma unroll
                             for (int e = 0; e < 8; e += 2)
-                                qkv_rotate(qr, s_inv_freq, pos_base, m0 + rr, col + e, f[e], f[e + 1]);
+                                qkv_rotate(qr, s_inv_freq, pos_base, m0 + rr, col0 + g * 8 + e, f[e], f[e + 1]);
                         }
                     }
                     if (acc_c) {
