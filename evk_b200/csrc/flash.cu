@@ -56,7 +56,8 @@ struct FlashCfg {
     static constexpr bool QT = QT_;
     static constexpr int Q_BYTES = FM * DH * 2;  // per tile
     static constexpr int KV_BYTES = FN * DH * 2;  // one K or V block
-    static constexpr int STAGES = NT == 4 ? 8 : NT == 2 ? (DH == 64 ? 5 : 2) : (DH == 64 ? 6 : 3);
+    static constexpr int STAGES =
+        NT == 4 ? 8 : NT == 2 ? (DH == 64 ? 5 : (FN == 64 ? 4 : 2)) : (DH == 64 ? 6 : 3);
     static constexpr uint32_t TMEM_COLS = 512;
     static constexpr int TSTRIDE = TMEM_COLS / NT;  // TMEM columns per tile
     // Per tile t: S (fp32, FN columns), O (fp32, DH columns) and P (FN 16-bit
@@ -82,7 +83,7 @@ struct FlashCfg {
 };
 static_assert(FlashCfg<64, 2, 128>::SMEM <= 227 * 1024 && FlashCfg<128, 2, 128>::SMEM <= 227 * 1024 &&
                   FlashCfg<64, 4, 64>::SMEM <= 227 * 1024 && FlashCfg<64, 2, 128, 0, true>::SMEM <= 227 * 1024 &&
-                  FlashCfg<64, 2, 128, 0, false, 2>::SMEM <= 227 * 1024,
+                  FlashCfg<64, 2, 128, 0, false, 2>::SMEM <= 227 * 1024 && FlashCfg<128, 2, 64>::SMEM <= 227 * 1024,
               "flash smem");
 
 // Phase trace (build with -DEVK_FLASH_TRACE only): clock64 stamps of CTA 0's
@@ -803,6 +804,18 @@ static int flash64_variant() {
     return v;
 }
 
+// Dh = 128 variant (EVKCU_FLASH128, for A/B measurement): 0 (default) two
+// tiles over 64-key blocks, S, O and P each in their own TMEM columns, so the
+// next S MMA need not wait for the PV MMA that reads P (C4-shaped causal bf16:
+// 174 us against 198 us); 1 two tiles over 128-key blocks with P written over S.
+static int flash128_variant() {
+    static const int v = [] {
+        const char* e = getenv("EVKCU_FLASH128");
+        return e ? atoi(e) : 0;
+    }();
+    return v;
+}
+
 int flash_attention_kv_strided(const void* q, const void* k, const void* v, void* o, uint32_t B, uint32_t N,
                                uint32_t H, uint32_t Hkv, uint32_t Dh, float scale, uint32_t flags, int dtype,
                                uint64_t kv_bstride, cudaStream_t st) {
@@ -851,8 +864,11 @@ int flash_attention_kv_strided(const void* q, const void* k, const void* v, void
                                                                  kv_bstride, st);
                 }
             }
-            return launch_flash_tc<T, 128, 2, 128, 0>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, kv_bstride,
-                                                      st);
+            if (flash128_variant() == 1)
+                return launch_flash_tc<T, 128, 2, 128, 0>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype,
+                                                          kv_bstride, st);
+            return launch_flash_tc<T, 128, 2, 64, 0>(q, k, v, o, B, N, H, Hkv, scale_log2, causal, dtype, kv_bstride,
+                                                     st);
         });
     }
     const uint64_t warps = (uint64_t)B * H * N;
