@@ -65,6 +65,8 @@ struct DeviceState {
     size_t ws_bytes[WS_COUNT] = {};
     bool pdl = true;  // programmatic dependent launch for the decode-path kernels
     bool plain_epilogue = false;  // GEMM: per-row stores instead of the staged TMA epilogue
+    int gemm_pair = -1;           // GEMM: paired-SM kernel (-1 by shape, 0 never, 1 whenever it applies)
+    int pair_clusters = 0;        // resident CTA pairs of the paired-SM GEMM (0: not yet queried)
 };
 // Returns the state of the current device, creating it on first use.
 DeviceState* state();

@@ -49,6 +49,7 @@ DeviceState* state() {
     cudaMemset(s->d_error, 0, sizeof(unsigned int));
     if (const char* v = getenv("EVKCU_DISABLE_PDL")) s->pdl = v[0] == '\0' || v[0] == '0';
     if (const char* v = getenv("EVKCU_GEMM_PLAIN_EPILOGUE")) s->plain_epilogue = v[0] != '\0' && v[0] != '0';
+    if (const char* v = getenv("EVKCU_GEMM_PAIR")) s->gemm_pair = atoi(v) ? 1 : 0;
     g_states[dev] = s;
     return s;
 }

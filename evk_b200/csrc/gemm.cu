@@ -387,6 +387,314 @@ __global__ void __launch_bounds__(kGemmThreads, CPS)
     }
 }
 
+// ------------------------------------------ paired-SM GEMM (M = 256 tiles) ----
+// Persistent kernel over 256 x 256 output tiles, one cluster of two CTAs on
+// neighbouring SMs per tile at a time.  CTA rank r of the pair loads A rows
+// [m0 + 128 r, +128) and B columns [n0 + 128 r, +128) into its own ring; the
+// rank-0 CTA issues one tcgen05.mma.cta_group::2 of M = 256, N = 256, K = 16
+// that reads both CTAs' operands, and each CTA's TMEM receives its 128 rows.
+// Per SM that halves the B operand held in shared memory and streamed from
+// L2 for the same tensor work as a 128 x 256 tile, and a 6-deep ring of 32 KB
+// stages fits beside the epilogue's staging.
+//
+// Roles (192 threads per CTA):
+//   warp 0 (both CTAs): TMA producer.  Each CTA's loads complete on the
+//     rank-0 CTA's full[s] barrier; the MMA's commit (CTA mask 0b11) frees
+//     the slot in both CTAs.
+//   warp 1 (rank 0): MMA issue into one of two 256-column TMEM accumulators,
+//     so the epilogue of tile j overlaps the mainloop of tile j + 1.
+//   warps 2-5 (both CTAs): epilogue of the CTA's 128 rows in 64-column boxes
+//     through two 16 KB staging buffers and TMA stores; the accumulator is
+//     released to the MMA warp (rank 0's tempty, 8 arrivals) as soon as its
+//     TMEM columns are in registers.
+// No load is multicast: every TMA load writes the issuing CTA's own shared
+// memory (only the MMA completion signal goes to both CTAs).  A variant that
+// passed the completion on to rank 1 with remote arrives instead measured
+// 745 against 1,380 TFLOP/s at 8192^3.  All waits are bounded; a CTA that gives up records a code
+// in the device error word and both CTAs meet at the final cluster barrier.
+constexpr int PR_ROWS = 128;  // rows (and B columns) per CTA of the pair
+constexpr int PR_A_BYTES = PR_ROWS * BK * 2;
+constexpr int PR_B_BYTES = PR_ROWS * BK * 2;
+constexpr int PR_STAGE_BYTES = PR_A_BYTES + PR_B_BYTES;
+constexpr int PR_STAGES = 6;
+constexpr int PR_BOX_BYTES = PR_ROWS * 128;  // one 128-row x 64-column box
+constexpr int PR_SMEM = PR_STAGES * PR_STAGE_BYTES + 2 * PR_BOX_BYTES + 1024 + 256;
+constexpr int kPairThreads = 192;
+constexpr uint32_t kTimeoutPair = 0x102;
+static_assert(PR_SMEM + 512 <= 232448, "paired GEMM shared memory exceeds the per-CTA limit");
+
+struct PairTile {
+    uint32_t m0, n0, z;
+};
+__device__ __forceinline__ PairTile pair_tile(uint32_t t, uint32_t mt, uint32_t nt) {
+    // Groups of 8 row tiles, row tile fastest: the pairs in flight share a
+    // few B column tiles and one group's A rows.
+    constexpr uint32_t G = 8;
+    const uint32_t per_batch = mt * nt;
+    PairTile p;
+    p.z = t / per_batch;
+    const uint32_t lin = t % per_batch, per_group = G * nt, grp = lin / per_group, first_m = grp * G;
+    const uint32_t gm = min(G, mt - first_m), in = lin % per_group;
+    p.m0 = (first_m + in % gm) * 256;
+    p.n0 = (in / gm) * 256;
+    return p;
+}
+
+template <typename T, bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmKc,
+                     const __grid_constant__ CUtensorMap tmVc, uint32_t M, uint32_t N, uint32_t K, uint32_t batch,
+                     int bcastA, int bcastB, int acc_c, uint32_t idesc, unsigned int* err, int gelu, QkvRope qr,
+                     int tma_c) {
+    __shared__ float s_inv_freq[128];
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + PR_STAGES * PR_A_BYTES;
+    uint8_t* stg = smem + PR_STAGES * PR_STAGE_BYTES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(stg + 2 * PR_BOX_BYTES);
+    uint64_t* empty = full + PR_STAGES;
+    uint64_t* tfull = empty + PR_STAGES;  // [2] accumulator buffer complete
+    uint64_t* tempty = tfull + 2;         // [2] accumulator buffer read (rank 0: 8 arrivals)
+    uint64_t* cbar = tempty + 2;          // [2] C box loaded into a staging buffer (acc_c)
+    uint32_t* s_tmem = reinterpret_cast<uint32_t*>(cbar + 2);
+    volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+    const uint32_t rank = cluster_ctarank();
+    const uint32_t pair = cluster_id_x(), npairs = cluster_count_x();
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t mt = (M + 255) / 256, nt = (N + 255) / 256;
+    const uint32_t total = mt * nt * batch;
+    const uint32_t num_kb = (K + BK - 1) / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PR_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 8);
+            mbar_init(&cbar[b], 1);
+        }
+        *s_abort = 0;
+        fence_barrier_init();
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        if (tma_c) prefetch_tmap(&tmC);
+        if (tma_c == 2) {
+            prefetch_tmap(&tmKc);
+            prefetch_tmap(&tmVc);
+        }
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(s_tmem, 512);
+        tmem_relinquish_pair();
+    }
+    qkv_fill_inv_freq(qr, s_inv_freq);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers exist before any remote arrive or load
+    tc_fence_after();
+    const uint32_t tmem = *s_tmem;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            bool ok = true;
+            for (uint32_t t = pair; ok && t < total; t += npairs) {
+                const PairTile tl = pair_tile(t, mt, nt);
+                const int za = bcastA ? 0 : (int)tl.z, zb = bcastB ? 0 : (int)tl.z;
+                const int am = (int)(tl.m0 + PR_ROWS * rank), bn = (int)(tl.n0 + PR_ROWS * rank);
+                for (uint32_t kb = 0; kb < num_kb; ++kb, ++it) {
+                    const int s = (int)(it % PR_STAGES);
+                    const uint32_t ph = (it / PR_STAGES) & 1;
+                    if (!mbar_wait_cluster(&empty[s], ph ^ 1, s_abort, err, kTimeoutPair)) {
+                        ok = false;
+                        break;
+                    }
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * PR_STAGE_BYTES);
+                    const uint32_t fb = map_shared_rank(&full[s], 0);
+                    const int k0 = (int)(kb * BK);
+                    uint8_t* a = sA + s * PR_A_BYTES;
+                    uint8_t* b = sB + s * PR_B_BYTES;
+                    if (!A_MN) {
+                        tma_load_3d_pair(a, &tmA, fb, k0, am, za);
+                    } else {
+                        tma_load_3d_pair(a, &tmA, fb, am, k0, za);
+                        tma_load_3d_pair(a + 8192, &tmA, fb, am + 64, k0, za);
+                    }
+                    if (!B_MN) {
+                        tma_load_3d_pair(b, &tmB, fb, k0, bn, zb);
+                    } else {
+                        tma_load_3d_pair(b, &tmB, fb, bn, k0, zb);
+                        tma_load_3d_pair(b + 8192, &tmB, fb, bn + 64, k0, zb);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (rank == 0 && lane == 0) {
+            uint32_t it = 0, j = 0;
+            bool ok = true;
+            for (uint32_t t = pair; ok && t < total; t += npairs, ++j) {
+                const uint32_t buf = j & 1, use = j >> 1;
+                if (!mbar_wait_cluster(&tempty[buf], (use & 1) ^ 1, s_abort, err, kTimeoutPair)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + buf * 256;
+                for (uint32_t kb = 0; kb < num_kb; ++kb, ++it) {
+                    const int s = (int)(it % PR_STAGES);
+                    const uint32_t ph = (it / PR_STAGES) & 1;
+                    if (!mbar_wait(&full[s], ph, s_abort, err, kTimeoutPair)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(sA + s * PR_A_BYTES);
+                    const uint32_t b = smem_u32(sB + s * PR_B_BYTES);
+#pragma unroll
+                    for (int k = 0; k < BK / 16; ++k) {
+                        const uint64_t ad =
+                            A_MN ? make_sw128_desc(a + k * 2048, 8192, 1024) : make_sw128_desc(a + k * 32, 16, 1024);
+                        const uint64_t bd =
+                            B_MN ? make_sw128_desc(b + k * 2048, 8192, 1024) : make_sw128_desc(b + k * 32, 16, 1024);
+                        mma_f16_ss_pair(d, ad, bd, idesc, (kb | k) != 0);
+                    }
+                    mma_commit_pair_mask(&empty[s], 3);  // the slot is free in both CTAs
+                }
+                if (ok) mma_commit_pair_mask(&tfull[buf], 3);
+            }
+        }
+    } else {
+        const int q = warp & 3;                 // TMEM lane quarter of this warp
+        const uint32_t rr = q * 32 + lane;      // row within the CTA's 128 rows
+        const bool leader = warp == 2 && lane == 0;
+        const uint32_t pos_base = qr.q ? (qr.d_pos ? *qr.d_pos : qr.pos0) : 0u;
+        const uint32_t qk_cols = (qr.Hq + qr.Hk) * qr.Dh;
+        uint32_t nbox = 0, j = 0;
+        for (uint32_t t = pair; t < total; t += npairs, ++j) {
+            const PairTile tl = pair_tile(t, mt, nt);
+            const uint32_t buf = j & 1, use = j >> 1;
+            int got = 0;
+            if (lane == 0) {
+                got = (int)mbar_wait_cluster(&tfull[buf], use & 1, s_abort, err, kTimeoutPair);
+            }
+            if (!__shfl_sync(0xffffffffu, got, 0)) break;
+            tc_fence_after();
+            const uint32_t mrow0 = tl.m0 + PR_ROWS * rank;  // this CTA's first output row
+            const uint32_t rpos = tma_c == 2 ? pos_base + (mrow0 + rr) % qr.S : 0u;
+            const float2* rtab =
+                (tma_c == 2 && qr.cs && rpos < qr.cs_len) ? qr.cs + (uint64_t)rpos * (qr.Dh >> 1) : nullptr;
+            bool go = true;
+#pragma unroll 1
+            for (int bx = 0; go && bx < 4; ++bx, ++nbox) {
+                const uint32_t sb = nbox & 1;
+                uint8_t* box = stg + sb * PR_BOX_BYTES;
+                const uint32_t col0 = tl.n0 + 64 * bx;
+                uint32_t r0[32], r1[32];
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + buf * 256 + bx * 64;
+                tmem_ld32(ta, r0);
+                tmem_ld32(ta + 32, r1);
+                tmem_wait_ld();
+                if (bx == 3) {
+                    // The accumulator buffer is in registers: hand it back.
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        if (rank == 0) mbar_arrive(&tempty[buf]);
+                        else mbar_arrive_remote(map_shared_rank(&tempty[buf], 0));
+                    }
+                }
+                // The store issued from this buffer two boxes ago has read it.
+                if (leader) tma_store_wait_read<1>();
+                named_barrier(1, 128);
+                if (acc_c) {
+                    if (leader) {
+                        mbar_arrive_expect_tx(&cbar[sb], (uint32_t)PR_BOX_BYTES);
+                        tma_load_3d(box, &tmC, &cbar[sb], (int)col0, (int)mrow0, (int)tl.z);
+                    }
+                    const int ok =
+                        __shfl_sync(0xffffffffu,
+                                    lane == 0 ? (int)mbar_wait(&cbar[sb], (nbox >> 1) & 1, s_abort, err, kTimeoutPair)
+                                              : 0,
+                                    0);
+                    if (!ok) {
+                        if (leader) mbar_drain(&cbar[sb], (nbox >> 1) & 1);
+                        go = false;
+                        break;
+                    }
+                }
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(g < 4 ? r0[g * 8 + e] : r1[(g - 4) * 8 + e]);
+                    Vec8* p = reinterpret_cast<Vec8*>(box + rr * 128 + ((g ^ (rr & 7)) << 4));
+                    const uint32_t c = col0 + 8 * g;
+                    if (tma_c == 2 && c < qk_cols) {
+                        if (rtab) {
+                            const uint32_t pb = (c % qr.Dh) >> 1;
+                            const float4 t0 = __ldg(reinterpret_cast<const float4*>(rtab + pb));
+                            const float4 t1 = __ldg(reinterpret_cast<const float4*>(rtab + pb + 2));
+                            const float cs4[4] = {t0.x, t0.z, t1.x, t1.z}, sn4[4] = {t0.y, t0.w, t1.y, t1.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float a = f[2 * e] * cs4[e] - f[2 * e + 1] * sn4[e];
+                                const float b = f[2 * e] * sn4[e] + f[2 * e + 1] * cs4[e];
+                                f[2 * e] = a;
+                                f[2 * e + 1] = b;
+                            }
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 8; e += 2)
+                                qkv_rotate(qr, s_inv_freq, pos_base, mrow0 + rr, c + e, f[e], f[e + 1]);
+                        }
+                    }
+                    if (acc_c) {
+                        float o[8];
+                        unpack8<T>(ld_shared_vec8(p), o);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] += o[e];
+                    }
+                    if (gelu) {
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = gelu_f(f[e]);
+                    }
+                    st_shared_vec8(p, pack8<T>(f));
+                }
+                fence_proxy_async_smem();
+                named_barrier(1, 128);
+                if (leader && mrow0 < M && col0 < N) {
+                    if (tma_c != 2) {
+                        tma_store_3d(&tmC, box, (int)col0, (int)mrow0, (int)tl.z);
+                    } else {
+                        const uint32_t qcols = qr.Hq * qr.Dh, kcols = qr.Hk * qr.Dh;
+                        const int pos = (int)(pos_base + mrow0 % qr.S), b = (int)(mrow0 / qr.S);
+                        if (col0 < qcols)
+                            tma_store_3d(&tmC, box, (int)col0, (int)mrow0, 0);
+                        else if (col0 < qcols + kcols)
+                            tma_store_3d(&tmKc, box, (int)(col0 - qcols), pos, b);
+                        else
+                            tma_store_3d(&tmVc, box, (int)(col0 - qcols - kcols), pos, b);
+                    }
+                    tma_store_commit();
+                }
+            }
+            if (!go) break;
+        }
+        if (leader) tma_store_wait_all();
+        tc_fence_before();
+    }
+    __syncthreads();
+    cluster_sync_all();  // no CTA leaves while its pair may still touch its memory
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 512);
+    }
+}
+
 // --------------------------------------------------------- small-M GEMV ----
 // y[m, n] = sum_k x[m, k] * W[k, n]     (W row-major [K, N]; or [N, K] with
 // transpose_b, e.g. a tied-embedding LM head), for Mt <= 16 rows of x.
@@ -892,24 +1200,21 @@ int launch_gemv_tc(const T* X, const T* W, T* Y, uint32_t Mt, uint32_t K, uint32
                       idesc, partial, tickets, s->d_error, ep.gelu, am, ar, qr);
 }
 
-template <typename T, int BN, bool A_MN, bool B_MN, int CPS>
-int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch, uint32_t M, uint32_t N, uint32_t K,
-              uint64_t strideC, int bcastA, int bcastB, int acc, int is_bf16, int gelu, const QkvRope& qr,
-              cudaStream_t st) {
-    using Cfg = GemmCfg<BN, CPS>;
-    static_assert(Cfg::STAGES * Cfg::STAGE_BYTES >= BN * BM * 2, "C staging must fit in the ring");
-    // Staged (TMA) epilogue for plain C = A B (+ C) (GELU): a map of C with
-    // 64-column x 128-row boxes in the 128-byte swizzle.
-    CUtensorMap tc, tk, tv;
+// Tensor maps of the staged (TMA) epilogue, 64-column x 128-row boxes in the
+// 128-byte swizzle: the C map for plain C = A B (+ C) (GELU), or the q / K
+// cache / V cache maps of a prefill's fused QKV projection.  *tma_c receives
+// the epilogue kind: 1 plain, 2 fused QKV, 0 per-row stores (no maps).
+int make_c_maps(CUtensorMap& tc, CUtensorMap& tk, CUtensorMap& tv, void* C, uint32_t batch, uint32_t M, uint32_t N,
+                uint64_t strideC, const QkvRope& qr, int is_bf16, int* tma_c) {
     memset(&tc, 0, sizeof(tc));
     memset(&tk, 0, sizeof(tk));
     memset(&tv, 0, sizeof(tv));
     const int dt = is_bf16 ? EVKCU_BF16 : EVKCU_F16;
-    int tma_c = 0;
+    *tma_c = 0;
     if (!qr.q && !state()->plain_epilogue) {
         const int r = make_tmap_3d(&tc, C, N, M, batch, N, batch > 1 ? strideC : (uint64_t)M * N, 64, BM, dt);
         if (r) return r;
-        tma_c = 1;
+        *tma_c = 1;
     } else if (qr.q && !qr.d_pos && qr.S % BM == 0 && (qr.Hq * qr.Dh) % 64 == 0 && (qr.Hk * qr.Dh) % 64 == 0 &&
                batch == 1 && !state()->plain_epilogue) {
         // Fused QKV of a prefill: q [M, Hq * Dh]; caches [M / S, max_len, Hk * Dh].
@@ -918,8 +1223,20 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch
         if (!r) r = make_tmap_3d(&tk, qr.kc, kc, qr.max_len, nb, kc, kc * qr.max_len, 64, BM, dt);
         if (!r) r = make_tmap_3d(&tv, qr.vc, kc, qr.max_len, nb, kc, kc * qr.max_len, 64, BM, dt);
         if (r) return r;
-        tma_c = 2;
+        *tma_c = 2;
     }
+    return EVKCU_OK;
+}
+
+template <typename T, int BN, bool A_MN, bool B_MN, int CPS>
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch, uint32_t M, uint32_t N, uint32_t K,
+              uint64_t strideC, int bcastA, int bcastB, int acc, int is_bf16, int gelu, const QkvRope& qr,
+              cudaStream_t st) {
+    using Cfg = GemmCfg<BN, CPS>;
+    static_assert(Cfg::STAGES * Cfg::STAGE_BYTES >= BN * BM * 2, "C staging must fit in the ring");
+    CUtensorMap tc, tk, tv;
+    int tma_c = 0;
+    if (int r = make_c_maps(tc, tk, tv, C, batch, M, N, strideC, qr, is_bf16, &tma_c)) return r;
     static bool attr_set = false;
     auto kern = gemm_tc_kernel<T, BN, A_MN, B_MN, CPS>;
     if (!attr_set) {
@@ -931,6 +1248,53 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, T* C, uint32_t batch
     kern<<<grid, kGemmThreads, Cfg::SMEM, st>>>(ta, tb, tc, tk, tv, C, M, N, K, strideC, bcastA, bcastB, acc, idesc,
                                                 state()->d_error, gelu, qr, tma_c);
     return after_launch("evkcu_matmul(tcgen05)");
+}
+
+// Paired-SM GEMM: one persistent cluster of two CTAs per resident SM pair.
+// The staged epilogue is required (tma_c != 0).
+template <typename T, bool A_MN, bool B_MN>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& tk,
+                const CUtensorMap& tv, int tma_c, uint32_t batch, uint32_t M, uint32_t N, uint32_t K, int bcastA,
+                int bcastB, int acc, int is_bf16, int gelu, const QkvRope& qr, uint32_t clusters, cudaStream_t st) {
+    auto kern = gemm_pair_kernel<T, A_MN, B_MN>;
+    const uint32_t tiles = ((M + 255) / 256) * ((N + 255) / 256) * batch;
+    const uint32_t n = std::min(tiles, clusters);
+    const uint32_t idesc = make_idesc_f16(256, 256, is_bf16, A_MN, B_MN);
+    kern<<<2 * n, kPairThreads, PR_SMEM, st>>>(ta, tb, tc, tk, tv, M, N, K, batch, bcastA, bcastB, acc, idesc,
+                                               state()->d_error, gelu, qr, tma_c);
+    return after_launch("evkcu_matmul(tcgen05 pair)");
+}
+
+// Sets the shared-memory limit of every paired-GEMM instantiation and
+// returns how many CTA pairs are resident at once (0 if the device cannot
+// run the kernel).  Queried once per device.
+uint32_t pair_clusters() {
+    DeviceState* ds = state();
+    if (ds->pair_clusters) return ds->pair_clusters > 0 ? (uint32_t)ds->pair_clusters : 0u;
+    const void* kerns[] = {
+        (const void*)gemm_pair_kernel<__half, false, false>,         (const void*)gemm_pair_kernel<__half, false, true>,
+        (const void*)gemm_pair_kernel<__half, true, false>,          (const void*)gemm_pair_kernel<__half, true, true>,
+        (const void*)gemm_pair_kernel<__nv_bfloat16, false, false>, (const void*)gemm_pair_kernel<__nv_bfloat16, false, true>,
+        (const void*)gemm_pair_kernel<__nv_bfloat16, true, false>,  (const void*)gemm_pair_kernel<__nv_bfloat16, true, true>};
+    for (const void* k : kerns) {
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, PR_SMEM) != cudaSuccess) {
+            cudaGetLastError();
+            ds->pair_clusters = -1;
+            return 0;
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * (ds->sm_count / 2), 1, 1);
+    cfg.blockDim = dim3(kPairThreads, 1, 1);
+    cfg.dynamicSmemBytes = PR_SMEM;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kerns[1], &cfg) != cudaSuccess || n <= 0) {
+        cudaGetLastError();
+        ds->pair_clusters = -1;
+        return 0;
+    }
+    ds->pair_clusters = n;
+    return (uint32_t)n;
 }
 
 template <typename T, int BN, int CPS>
@@ -1039,6 +1403,11 @@ int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M,
 
     CUtensorMap mA, mB;
     const uint32_t zA = bA ? 1 : batch, zB = bB ? 1 : batch;
+    // Paired-SM kernel for large outputs: 256 x 256 tiles, at least one
+    // tile per resident pair.
+    const uint64_t pair_tiles = (uint64_t)((M + 255) / 256) * ((N + 255) / 256) * batch;
+    const bool pair_shape = ds->gemm_pair != 0 && !ds->plain_epilogue && M >= 256 &&
+                            (ds->gemm_pair == 1 || pair_tiles >= (uint64_t)(ds->sm_count / 2));
     int r;
     if (!ta)
         r = make_tmap_3d(&mA, A, K, M, zA, K, (zA > 1 ? stride_a : (uint64_t)M * K), BK, BM, dtype);
@@ -1051,6 +1420,33 @@ int matmul_ex(const void* A, const void* B, void* C, uint32_t batch, uint32_t M,
         r = make_tmap_3d(&mB, B, K, N, zB, K, (zB > 1 ? stride_b : (uint64_t)K * N), BK, BN, dtype);
     if (r) return r;
     const uint64_t sC = batch > 1 ? stride_c : 0;
+    if (pair_shape) {
+        const uint32_t clusters = pair_clusters();
+        CUtensorMap tc, tk, tv;
+        int tma_c = 0;
+        r = make_c_maps(tc, tk, tv, C, batch, M, N, sC, qr, bf, &tma_c);
+        if (r) return r;
+        if (clusters && tma_c) {
+            CUtensorMap mBp = mB;
+            if (tb) {  // K-major B: one CTA holds 128 rows of it
+                r = make_tmap_3d(&mBp, B, K, N, zB, K, (zB > 1 ? stride_b : (uint64_t)K * N), BK, 128, dtype);
+                if (r) return r;
+            }
+            return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
+                if (!ta && !tb)
+                    return launch_pair<T, false, true>(mA, mBp, tc, tk, tv, tma_c, batch, M, N, K, bA, bB, acc, bf,
+                                                       gelu, qr, clusters, st);
+                if (!ta && tb)
+                    return launch_pair<T, false, false>(mA, mBp, tc, tk, tv, tma_c, batch, M, N, K, bA, bB, acc, bf,
+                                                        gelu, qr, clusters, st);
+                if (ta && !tb)
+                    return launch_pair<T, true, true>(mA, mBp, tc, tk, tv, tma_c, batch, M, N, K, bA, bB, acc, bf,
+                                                      gelu, qr, clusters, st);
+                return launch_pair<T, true, false>(mA, mBp, tc, tk, tv, tma_c, batch, M, N, K, bA, bB, acc, bf, gelu,
+                                                   qr, clusters, st);
+            });
+        }
+    }
     return EVKCU_DISPATCH_DTYPE(dtype, T, [&] {
         if (BN == 256)
             return dispatch_major<T, 256>(ta, tb, mA, mB, (T*)C, batch, M, N, K, sC, bA, bB, acc, bf, gelu, qr, st);
@@ -1102,4 +1498,14 @@ extern "C" int evkcu_matmul(const void* A, const void* B, void* C, uint32_t batc
                             uint64_t stride_a, uint64_t stride_b, uint64_t stride_c, uint32_t flags, int dtype,
                             void* stream) {
     return matmul_ex(A, B, C, batch, M, K, N, stride_a, stride_b, stride_c, flags, dtype, 0, stream);
+}
+
+// Diagnostic export (not in the public header): CTA pairs of the paired-SM
+// GEMM resident at once on the current device; 0 if it cannot run there, -1
+// if EVKCU_GEMM_PAIR=0 turned it off.
+extern "C" int evkcu_debug_gemm_pair_clusters(void) {
+    DeviceState* ds = state();
+    if (!ds) return 0;
+    if (ds->gemm_pair == 0) return -1;
+    return (int)pair_clusters();
 }

@@ -67,6 +67,12 @@ CASES = [
     (1, 16, 1024, 4096, 0, 0, 0, ""),  # GEMV, 16 rows
     (1, 3, 512, 32000, 0, 1, 0, ""),  # GEMV, transposed B (tied LM head)
     (4, 2, 512, 1024, 0, 0, 0, "b"),  # GEMV over a broadcast weight
+    # M >= 256: the paired-SM kernel's shapes when it is forced on
+    # (tests/test_gpu_gemm_pair.py); ragged M, N and K, every operand layout
+    (1, 1000, 72, 776, 0, 0, 1, ""),
+    (1, 520, 136, 264, 0, 1, 1, ""),
+    (3, 256, 128, 256, 1, 1, 0, "a"),
+    (2, 304, 200, 520, 1, 0, 1, "b"),
 ]
 
 
