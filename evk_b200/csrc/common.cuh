@@ -217,14 +217,13 @@ int gemv_argmax(const void* X, const void* W, uint32_t Mt, uint32_t K, uint32_t 
 // Row-parallel decode GEMV fused with the tensor-parallel all-reduce and the
 // residual add: y[m, :] += sum over ranks of (x_r[m, :] . W_r).  Each slab's
 // final fp32 partial is pushed into every rank's buf (plain stores over
-// NVLink peer mappings), a per-slab flag carrying *epoch is published to
-// every rank, and after a bounded wait for all ranks' flags each rank sums
-// the partials in rank order (identical on every rank) and adds them to y.
-// buf[q]: rank q's [2][tp][16][N] fp32 (double-buffered by call-site
-// parity); flags[q]: rank q's [call sites][slabs][tp] words.
+// NVLink peer mappings) as (value, flag) pairs, the flag being
+// *epoch * 256 + callsite + 1; each rank polls its own buf (bounded) until
+// every rank's pairs carry the flag, sums them in rank order (identical on
+// every rank) and adds the sum to y.  buf[q]: rank q's [2][tp][16][N] pairs
+// (double-buffered by call-site parity); callsite < 255.
 struct GemvAllReduce {
-    float* buf[8] = {};
-    uint32_t* flags[8] = {};
+    uint2* buf[8] = {};
     const uint32_t* epoch = nullptr;
     uint32_t tp = 0, rank = 0, callsite = 0;
 };

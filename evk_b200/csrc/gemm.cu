@@ -921,75 +921,80 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
     if (ar.tp) gemv_allreduce_tail<T>(reinterpret_cast<const float*>(smem), Y, Mt, N, n0, ar, err);
 }
 
-// Tensor-parallel all-reduce of one slab's fp32 partial (see GemvAllReduce):
-// push to every rank, publish the flag, wait (bounded) for every rank's flag,
-// sum in rank order, add to the residual y.
+// Tensor-parallel all-reduce of one slab's fp32 partial (see GemvAllReduce),
+// in the low-latency form of a flag beside every value: each 16-byte store
+// carries two (value, flag) pairs, and an aligned 8-byte pair is written and
+// read as one unit, so a reader that sees the expected flag also sees the
+// value, with no memory fence on either side.  The flag is unique per decode
+// step and call site (step * 256 + callsite + 1; never 0, the buffer's
+// initial contents).
+//   1. push this rank's partial into slot [parity][rank] of every rank's
+//      buffer (peer memory over NVLink);
+//   2. poll this rank's own buffer (bounded) until every rank's slot shows
+//      the flag, summing the values in rank order (the same on every rank,
+//      so the replicated residual stays bit-identical);
+//   3. add the sum to the residual y.
+// A rank cannot get two all-reduces ahead of another (each needs every
+// rank's contribution), so a slot is rewritten only after its readers are
+// done with it.
+__device__ __forceinline__ void st_pair2(uint2* dst, float v0, float v1, uint32_t flag) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(__float_as_uint(v0)), "r"(flag),
+                 "r"(__float_as_uint(v1)), "r"(flag)
+                 : "memory");
+}
+__device__ __forceinline__ uint4 ld_pair2(const uint2* src) {
+    uint4 r;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(src)
+                 : "memory");
+    return r;
+}
+
 template <typename T>
 __device__ void gemv_allreduce_tail(const float* s_val, T* __restrict__ Y, uint32_t Mt, uint32_t N, uint32_t n0,
                                     const GemvAllReduce& ar, unsigned int* err) {
-    __shared__ int s_ok;
+    __shared__ int s_fail;
+    if (threadIdx.x == 0) s_fail = 0;
     __syncthreads();  // s_val complete
-    const uint32_t slab = blockIdx.x, slabs = gridDim.x;
     const uint32_t par = ar.callsite & 1;
-    const uint32_t ep = *ar.epoch;
-    const uint32_t groups = Mt * GV_COLS / 4;
-    // 1. This rank's partial into slot [par][rank] of every rank's buffer.
+    const uint32_t flag = *ar.epoch * 256u + ar.callsite + 1u;
+    const uint32_t groups = Mt * GV_COLS / 2;
     for (uint32_t g = threadIdx.x; g < groups; g += blockDim.x) {
-        const uint32_t m = (g * 4) / GV_COLS, c = (g * 4) % GV_COLS;
-        const float4 v = *reinterpret_cast<const float4*>(s_val + m * GV_COLS + c);
+        const uint32_t m = (g * 2) / GV_COLS, c = (g * 2) % GV_COLS;
+        if (n0 + c >= N) continue;
+        const float2 v = *reinterpret_cast<const float2*>(s_val + m * GV_COLS + c);
         const uint64_t off = ((uint64_t)(par * ar.tp + ar.rank) * GV_MMA_N + m) * N + n0 + c;
-        for (uint32_t q = 0; q < ar.tp; ++q)
-            if (n0 + c < N) *reinterpret_cast<float4*>(ar.buf[q] + off) = v;
+        for (uint32_t q = 0; q < ar.tp; ++q) st_pair2(ar.buf[q] + off, v.x, v.y, flag);
     }
-    __threadfence_system();
-    __syncthreads();
-    const uint64_t fslot = ((uint64_t)ar.callsite * slabs + slab) * ar.tp;
-    if (threadIdx.x == 0) {
-        for (uint32_t q = 0; q < ar.tp; ++q)
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ar.flags[q] + fslot + ar.rank), "r"(ep)
-                         : "memory");
-        // 2. Every rank's partial has landed here once its flag shows ep.
-        int ok = 1;
-        const long long t0 = clock64();
-        for (uint32_t q = 0; q < ar.tp && ok; ++q) {
-            uint32_t f;
-            while (true) {
-                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(f) : "l"(ar.flags[ar.rank] + fslot + q)
-                             : "memory");
-                if (f == ep) break;
-                if (clock64() - t0 > kSpinLimitCycles / 2 || *reinterpret_cast<volatile unsigned int*>(err)) {
-                    atomicCAS(err, 0u, 0x302u);
-                    ok = 0;
-                    break;
-                }
-                __nanosleep(20);
-            }
-        }
-        s_ok = ok;
-    }
-    __syncthreads();
-    if (!s_ok) return;
-    __threadfence();
-    // 3. Sum in rank order (the same on every rank) and add to the residual.
-    const float* mine = ar.buf[ar.rank];
+    const uint2* mine = ar.buf[ar.rank];
+    const long long t0 = clock64();
     for (uint32_t g = threadIdx.x; g < groups; g += blockDim.x) {
-        const uint32_t m = (g * 4) / GV_COLS, c = (g * 4) % GV_COLS, n = n0 + c;
+        const uint32_t m = (g * 2) / GV_COLS, c = (g * 2) % GV_COLS, n = n0 + c;
         if (n >= N) continue;
-        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float a0 = 0.0f, a1 = 0.0f;
         for (uint32_t q = 0; q < ar.tp; ++q) {
-            const float4 v = __ldcv(reinterpret_cast<const float4*>(
-                mine + ((uint64_t)(par * ar.tp + q) * GV_MMA_N + m) * N + n));
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
+            const uint2* src = mine + ((uint64_t)(par * ar.tp + q) * GV_MMA_N + m) * N + n;
+            uint4 w = ld_pair2(src);
+            for (uint32_t spin = 0; w.y != flag || w.w != flag; ++spin) {
+                if ((spin & 31) == 31) {
+                    if (*reinterpret_cast<volatile int*>(&s_fail) || *reinterpret_cast<volatile unsigned int*>(err)) {
+                        s_fail = 1;
+                        return;
+                    }
+                    if (clock64() - t0 > kSpinLimitCycles / 2) {
+                        atomicCAS(err, 0u, 0x302u);
+                        s_fail = 1;
+                        return;
+                    }
+                }
+                w = ld_pair2(src);
+            }
+            a0 += __uint_as_float(w.x);
+            a1 += __uint_as_float(w.z);
         }
-        const float a[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            T* y = Y + (uint64_t)m * N + n + e;
-            *y = Elem<T>::from_f(Elem<T>::to_f(*y) + a[e]);
-        }
+        T* y = Y + (uint64_t)m * N + n;
+        y[0] = Elem<T>::from_f(Elem<T>::to_f(y[0]) + a0);
+        y[1] = Elem<T>::from_f(Elem<T>::to_f(y[1]) + a1);
     }
 }
 

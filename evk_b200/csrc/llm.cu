@@ -149,9 +149,8 @@ struct evkcu_llm {
     uint32_t *d_pos = nullptr, *d_len = nullptr, *d_epoch = nullptr;
     float2* rope_cs = nullptr;  // (cos, sin) per position and rotation pair
     // Fused all-reduce of the decode Wo / W2 projections (tp > 1): this
-    // rank's partial buffer and flags, and every rank's through IPC.
-    float* ar_buf = nullptr;
-    uint32_t* ar_flags = nullptr;
+    // rank's (value, flag) buffer, and every rank's through IPC.
+    uint2* ar_buf = nullptr;
     GemvAllReduce ar{};
     bool ar_ready = false;
     std::vector<void*> ipc_opened;
@@ -190,6 +189,12 @@ ncclDataType_t nccl_type(int dtype) { return dtype == EVKCU_BF16 ? ncclBfloat16 
         if (_r) return _r; \
     } while (0)
 
+// Largest rows x d_model for the fused decode all-reduce.  Its (value, flag)
+// pairs of fp32 partials carry 4x the bytes of NCCL's 16-bit all-reduce;
+// measured at tp = 2 (decode ms per step, fused / NCCL): C3 1 x 512 0.235 /
+// 0.322, C4 8 x 2048 1.78 / 2.22, C5 16 x 4096 7.19 / 6.91.
+constexpr uint64_t kFusedArMaxElems = 32768;
+
 // Wo / W2 product into the residual.  On one GPU acc_c fuses the add; with
 // tensor parallelism the product is a partial sum, summed across ranks first.
 int proj_residual(evkcu_llm* m, const void* a, const void* w, uint32_t rows, uint32_t K, bool decode,
@@ -197,7 +202,7 @@ int proj_residual(evkcu_llm* m, const void* a, const void* w, uint32_t rows, uin
     const uint32_t D = m->cfg.d_model;
     const int dt = m->cfg.dtype;
     if (m->cfg.tp_size == 1) return evkcu_matmul(a, w, m->x, 1, rows, K, D, 0, 0, 0, EVKCU_MM_ACC_C, dt, st);
-    if (decode && rows <= 16 && m->ar_ready) {
+    if (decode && rows <= 16 && m->ar_ready && (uint64_t)rows * D <= kFusedArMaxElems) {
         // GEMV + all-reduce over NVLink peer memory + residual add, one kernel.
         GemvAllReduce ar = m->ar;
         ar.callsite = callsite;
@@ -381,8 +386,8 @@ extern "C" int evkcu_comm_destroy(void* comm) {
     return EVKCU_OK;
 }
 
-// Exchanges CUDA IPC handles of every rank's all-reduce buffer and flags
-// (ncclAllGather of the 2 x 64-byte handles), maps the peers' into this
+// Exchanges CUDA IPC handles of every rank's all-reduce buffer
+// (ncclAllGather of the 64-byte handles), maps the peers' into this
 // process, then agrees across ranks (ncclAllReduce, min) on whether every rank
 // succeeded and has the fused path switched on.  Every rank issues the same
 // two collectives whatever happens locally, so a failure on one rank (or
@@ -392,15 +397,15 @@ extern "C" int evkcu_comm_destroy(void* comm) {
 static void setup_allreduce(evkcu_llm* m, char* xch) {
     const uint32_t t = m->cfg.tp_size, rank = m->cfg.tp_rank;
     if (t > 8) return;  // same decision on every rank: t is shared
-    bool ok = m->ar_buf && m->ar_flags && getenv("EVKCU_DISABLE_FUSED_ALLREDUCE") == nullptr;
-    const size_t fbytes = (size_t)2 * m->cfg.layers * ((m->cfg.d_model + 127) / 128) * t * sizeof(uint32_t);
-    ok = ok && cudaMemset(m->ar_flags, 0, fbytes) == cudaSuccess;
-    cudaIpcMemHandle_t h[2];
+    // Flags are step * 256 + callsite + 1 with callsite < 2 * layers.
+    bool ok = m->ar_buf && 2 * m->cfg.layers < 255 && getenv("EVKCU_DISABLE_FUSED_ALLREDUCE") == nullptr;
+    const size_t bbytes = (size_t)2 * t * 16 * m->cfg.d_model * sizeof(uint2);
+    ok = ok && cudaMemset(m->ar_buf, 0, bbytes) == cudaSuccess;
+    cudaIpcMemHandle_t h[1];
     std::memset(h, 0, sizeof(h));
-    ok = ok && cudaIpcGetMemHandle(&h[0], m->ar_buf) == cudaSuccess &&
-         cudaIpcGetMemHandle(&h[1], m->ar_flags) == cudaSuccess;
+    ok = ok && cudaIpcGetMemHandle(&h[0], m->ar_buf) == cudaSuccess;
     cudaGetLastError();
-    std::vector<cudaIpcMemHandle_t> all(2 * t);
+    std::vector<cudaIpcMemHandle_t> all(t);
     bool comm_ok = cudaMemcpy(xch, h, sizeof(h), cudaMemcpyHostToDevice) == cudaSuccess &&
                    ncclAllGather(xch, xch + sizeof(h), sizeof(h), ncclUint8, m->comm, 0) == ncclSuccess &&
                    cudaStreamSynchronize(0) == cudaSuccess &&
@@ -413,16 +418,12 @@ static void setup_allreduce(evkcu_llm* m, char* xch) {
     for (uint32_t q = 0; q < t && ok; ++q) {
         if (q == rank) {
             ar.buf[q] = m->ar_buf;
-            ar.flags[q] = m->ar_flags;
             continue;
         }
-        void *pb = nullptr, *pf = nullptr;
-        ok = cudaIpcOpenMemHandle(&pb, all[2 * q], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+        void* pb = nullptr;
+        ok = cudaIpcOpenMemHandle(&pb, all[q], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
         if (ok) m->ipc_opened.push_back(pb);
-        ok = ok && cudaIpcOpenMemHandle(&pf, all[2 * q + 1], cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
-        if (ok) m->ipc_opened.push_back(pf);
-        ar.buf[q] = (float*)pb;
-        ar.flags[q] = (uint32_t*)pf;
+        ar.buf[q] = (uint2*)pb;
     }
     cudaGetLastError();
     // Agreement: the fused path is used only if it is ready on every rank.
@@ -500,12 +501,10 @@ extern "C" int evkcu_llm_create(const evkcu_llm_config* cfg, void* comm, evkcu_l
     }
     A((void**)&m->d_pos, 4 * sizeof(uint32_t));  // position, length, decode-step counter
     A((void**)&m->rope_cs, (size_t)c.max_seq * (Dh / 2) * sizeof(float2));
-    const uint32_t slabs = (uint32_t)((D + 127) / 128);
     char* xch = nullptr;  // handle exchange / agreement word of setup_allreduce
     if (t > 1) {
         A((void**)&xch, (size_t)128 * (t + 1) + 4);
-        A((void**)&m->ar_buf, (size_t)2 * t * 16 * D * sizeof(float));
-        A((void**)&m->ar_flags, (size_t)2 * c.layers * slabs * t * sizeof(uint32_t));
+        A((void**)&m->ar_buf, (size_t)2 * t * 16 * D * sizeof(uint2));
     }
     A((void**)&m->gin, (size_t)c.max_batch * 4);
     A((void**)&m->gout, (size_t)c.max_batch * 4);
