@@ -265,6 +265,12 @@ def profile_leg(leg):
         o = torch.empty_like(q)
         for _ in range(5):
             evk.flash_attention(q, k, v, o, heads=H, causal=CAUSAL)
+    elif leg == "flash128":
+        # C4 prefill attention: B=8, H=16, S=2048, Dh=128, causal, bf16
+        q, k, v = (torch.randn(8, 2048, 16 * 128, device="cuda").bfloat16() for _ in range(3))
+        o = torch.empty_like(q)
+        for _ in range(5):
+            evk.flash_attention(q, k, v, o, heads=16, causal=True)
     elif leg == "gemm":
         a, b = (torch.randn(8192, 8192, device="cuda").bfloat16() for _ in range(2))
         c = torch.empty_like(a)
@@ -349,7 +355,7 @@ def main():
     ap.add_argument("--impl", default="evk_b200", choices=["evk_b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true")
-    ap.add_argument("--profile-leg", choices=["flash", "gemm", "gemv", "decode", "llm-decode"], default=None,
+    ap.add_argument("--profile-leg", choices=["flash", "flash128", "gemm", "gemv", "decode", "llm-decode"], default=None,
                     help="run a few launches of one leg and exit (for ncu captures; prints no JSON)")
     ap.add_argument("--gemm-shapes", action="store_true",
                     help="print TFLOP/s of the prefill projection GEMM shapes (one JSON line each) and exit")
