@@ -550,7 +550,7 @@ def main():
         "clocks": clocks.summary(),
         "extra": extra,
     }
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and ws == 1:  # the CPU baseline is timed at N = 1 only
         line["cpu_baseline"] = dict(cpu_baseline(budget_s=10.0), kind="port")
     print(json.dumps(line), flush=True)
     if ws > 1:
