@@ -145,6 +145,40 @@ def cpu_baseline(budget_s: float = 10.0, threads: int | None = None):
     }
 
 
+def cpu_extra():
+    """The CPU oracle on the other configurations the survey plans a CPU
+    baseline for: C1 (matmul 1024^3, fp16) and C3 decode steps (the oracle
+    decoder, tests/llm_ref.py: KV-cached, batch 1, after a 128-token prompt).
+    A few seconds each, on all host threads."""
+    import numpy as np
+
+    import oracle
+
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    from llm_ref import RefModel
+
+    n = 1024
+    a, b = oracle.normal(n * n, 1), oracle.normal(n * n, 2)
+    c = np.empty(n * n, np.uint16)
+    oracle.matmul(a, b, c, 1, n, n, n, 0, 0, 0, 0, 0)
+    reps, t0 = 0, time.perf_counter()
+    while reps < 2 or time.perf_counter() - t0 < 2.0:
+        oracle.matmul(a, b, c, 1, n, n, n, 0, 0, 0, 0, 0)
+        reps += 1
+    c1 = 2.0 * n ** 3 * reps / (time.perf_counter() - t0) / 1e9
+    m = RefModel(6, 512, 8, 2048, 32000, True, dtype=0, seed=42)
+    prompt = oracle.uniform_ids(128, 7, 0, 32000, 4).astype(np.int64).reshape(1, 128)
+    logits = m.start(prompt, 128 + 257)
+    ids = m.greedy(logits)
+    steps, t0 = 0, time.perf_counter()
+    while steps < 256 and (steps < 3 or time.perf_counter() - t0 < 3.0):
+        ids = m.greedy(m.step(ids))
+        steps += 1
+    c3 = (time.perf_counter() - t0) / steps * 1e3
+    return {"c1_matmul_gflops": round(c1, 2), "c3_decode_ms_per_step": round(c3, 2),
+            "sample": f"C1: {reps} matmuls; C3: {steps} decode steps after a 128-token prompt"}
+
+
 def run_reference(args):
     ws, rank, _ = dist_env()
     if rank != 0:
@@ -552,6 +586,8 @@ def main():
     }
     if not args.no_cpu_baseline and ws == 1:  # the CPU baseline is timed at N = 1 only
         line["cpu_baseline"] = dict(cpu_baseline(budget_s=10.0), kind="port")
+        if not args.no_extra:
+            line["cpu_baseline"]["extra"] = cpu_extra()
     print(json.dumps(line), flush=True)
     if ws > 1:
         torch.distributed.destroy_process_group()
