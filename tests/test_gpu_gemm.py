@@ -122,3 +122,48 @@ def test_matmul_rejects_bad_rows():
     c = torch.empty(64, 64, device="cuda").half()
     with pytest.raises(evk_b200.EvkcuError):
         ev().matmul(a, b, c)
+
+
+def _random_cases(n=14, seed=20261202):
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n):
+        batch = int(rng.choice([1, 1, 2, 3]))
+        M = int(rng.integers(1, 1600))
+        K = 8 * int(rng.integers(1, 300))
+        N = 8 * int(rng.integers(1, 260))
+        ta, tb, acc = (int(x) for x in rng.integers(0, 2, 3))
+        if ta:
+            M = max(8, M - M % 8)  # transpose_a: M is the contiguous dimension
+        bc = str(rng.choice(["", "", "a", "b"])) if batch > 1 else ""
+        out.append((batch, M, K, N, ta, tb, acc, bc))
+    return out
+
+
+RANDOM_CASES = _random_cases()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("case", RANDOM_CASES, ids=[str(c) for c in RANDOM_CASES])
+def test_matmul_random_shapes_vs_torch_fp32(dtype, case):
+    """Seeded random shapes (ragged M, N, K; every operand layout; batch
+    broadcast; C +=) against a torch fp32 product rounded once to the storage
+    type, with the same bounds as the large-shape test."""
+    batch, M, K, N, ta, tb, acc, bc = case
+    g = torch.Generator(device="cuda").manual_seed(M * 7919 + N * 31 + K)
+    ba = 1 if bc == "a" else batch
+    bb = 1 if bc == "b" else batch
+    a = torch.randn(ba, *((K, M) if ta else (M, K)), device="cuda", generator=g).to(dtype)
+    b = torch.randn(bb, *((N, K) if tb else (K, N)), device="cuda", generator=g).to(dtype)
+    c = torch.randn(batch, M, N, device="cuda", generator=g).to(dtype)
+    c0 = c.float().clone()
+    ev().matmul(a, b, c, bool(ta), bool(tb), bool(acc))
+    A = a.float().transpose(1, 2) if ta else a.float()
+    B = b.float().transpose(1, 2) if tb else b.float()
+    ref = torch.matmul(A.expand(batch, M, K), B.expand(batch, K, N)) + (c0 if acc else 0.0)
+    ref = ref.to(dtype).float()
+    err = c.float() - ref
+    rel = (err.norm() / ref.norm()).item()
+    tol_elem = 2e-2 + (2 ** -10 if dtype == torch.float16 else 2 ** -7) * ref.abs()
+    assert rel <= (1e-3 if dtype == torch.float16 else 2e-3), f"rel-L2 {rel}"
+    assert bool((err.abs() <= tol_elem).all()), f"max abs err {err.abs().max().item()}"
