@@ -211,3 +211,44 @@ def test_single_query_attention_ignores_cache_rows_past_length(dtype):
                                 dev(vc.ravel(), dtype).view(B, L, H * Dh), out, H, cur)
     assert bool(torch.isfinite(out.float()).all())
     assert_close(u16(out).ravel(), r, dc, rel_l2=1e-3 if dc == 0 else 4e-3, what="decode with NaN tail")
+
+
+def _flash_random_cases(n=12, seed=1202):
+    rng = np.random.default_rng(seed)
+    out = []
+    for i in range(n):
+        Dh = int(rng.choice([64, 64, 128, 128, 96]))  # 96: the one-warp-per-row kernel
+        Hkv = int(rng.choice([1, 2, 4]))
+        H = Hkv * int(rng.choice([1, 2, 4]))
+        B = int(rng.integers(1, 4))
+        N = int(rng.integers(16, 700 if Dh == 96 else 1500))
+        causal = bool(rng.integers(0, 2))
+        out.append((B, N, H, Hkv, Dh, causal))
+    return out
+
+
+FLASH_RANDOM = _flash_random_cases()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("case", FLASH_RANDOM, ids=[str(c) for c in FLASH_RANDOM])
+def test_flash_random_shapes_vs_torch(dtype, case):
+    """Seeded random shapes (ragged sequence lengths, MQA / GQA / MHA, Dh 64,
+    128 and 96, causal or not) against torch fp32 attention, with the bounds
+    of the full-size test."""
+    B, N, H, Hkv, Dh, causal = case
+    g = torch.Generator(device="cuda").manual_seed(N * 131 + H * 7 + Dh)
+    q = torch.randn(B, N, H * Dh, device="cuda", generator=g).to(dtype)
+    k = torch.randn(B, N, Hkv * Dh, device="cuda", generator=g).to(dtype)
+    v = torch.randn(B, N, Hkv * Dh, device="cuda", generator=g).to(dtype)
+    o = torch.empty_like(q)
+    ev().flash_attention(q, k, v, o, heads=H, causal=causal)
+    qf = q.float().view(B, N, H, Dh).transpose(1, 2)
+    kf = k.float().view(B, N, Hkv, Dh).transpose(1, 2).repeat_interleave(H // Hkv, dim=1)
+    vf = v.float().view(B, N, Hkv, Dh).transpose(1, 2).repeat_interleave(H // Hkv, dim=1)
+    ref = torch.nn.functional.scaled_dot_product_attention(qf, kf, vf, is_causal=causal)
+    ref = ref.transpose(1, 2).reshape(B, N, H * Dh)
+    err = o.float() - ref
+    rel = (err.norm() / ref.norm()).item()
+    assert rel <= (1e-3 if dtype == torch.float16 else 8e-3), rel
+    assert err.abs().max().item() <= (2e-2 if dtype == torch.float16 else 6e-2)
