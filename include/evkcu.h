@@ -347,10 +347,11 @@ int evkcu_llm_prefill(evkcu_llm* m, const uint32_t* tokens, uint32_t B, uint32_t
 int evkcu_llm_decode(evkcu_llm* m, const uint32_t* ids, uint32_t* next_ids, void* logits_out, void* stream);
 /* Number of cached positions (prefill length + decode steps).  Host value. */
 uint32_t evkcu_llm_length(const evkcu_llm* m);
-/* 1 when the decode Wo / W2 all-reduce of this tensor-parallel model runs
+/* 1 when the decode Wo / W2 all-reduce of this tensor-parallel model can run
  * fused over peer memory (every rank mapped its peers and none set
  * EVKCU_DISABLE_FUSED_ALLREDUCE; the ranks agree at creation), 0 when it
- * uses NCCL.  Host value.                                                    */
+ * uses NCCL.  Even when 1, calls of more than 32,768 elements (batch rows x
+ * d_model) use NCCL.  Host value.                                            */
 uint32_t evkcu_llm_fused_allreduce(const evkcu_llm* m);
 
 #ifdef __cplusplus
