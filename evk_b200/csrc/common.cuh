@@ -222,10 +222,13 @@ int gemv_argmax(const void* X, const void* W, uint32_t Mt, uint32_t K, uint32_t 
 // every rank's pairs carry the flag, sums them in rank order (identical on
 // every rank) and adds the sum to y.  buf[q]: rank q's [2][tp][16][N] pairs
 // (double-buffered by call-site parity); callsite < 255.
+// With half = 1 the partials travel rounded to the storage type, two values
+// per (pair, flag) word (half the bytes; the same numerics as an all-reduce
+// of 16-bit partials).
 struct GemvAllReduce {
     uint2* buf[8] = {};
     const uint32_t* epoch = nullptr;
-    uint32_t tp = 0, rank = 0, callsite = 0;
+    uint32_t tp = 0, rank = 0, callsite = 0, half = 0;
 };
 int gemv_allreduce_residual(const void* X, const void* W, void* Y, uint32_t Mt, uint32_t K, uint32_t N,
                             const GemvAllReduce& ar, int dtype, cudaStream_t st);

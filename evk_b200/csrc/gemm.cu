@@ -958,6 +958,56 @@ __device__ void gemv_allreduce_tail(const float* s_val, T* __restrict__ Y, uint3
     __syncthreads();  // s_val complete
     const uint32_t par = ar.callsite & 1;
     const uint32_t flag = *ar.epoch * 256u + ar.callsite + 1u;
+    if (ar.half) {
+        // Four columns per 16-byte word: {v0 v1 | flag | v2 v3 | flag}.
+        const uint32_t g4 = Mt * GV_COLS / 4, NW = N / 2;  // NW: words of one row
+        using T2 = typename Elem<T>::T2;
+        for (uint32_t g = threadIdx.x; g < g4; g += blockDim.x) {
+            const uint32_t m = (g * 4) / GV_COLS, c = (g * 4) % GV_COLS;
+            if (n0 + c >= N) continue;
+            const float4 v = *reinterpret_cast<const float4*>(s_val + m * GV_COLS + c);
+            const T2 lo = Elem<T>::from_f2(v.x, v.y), hi = Elem<T>::from_f2(v.z, v.w);
+            const uint64_t off = ((uint64_t)(par * ar.tp + ar.rank) * GV_MMA_N + m) * NW + (n0 + c) / 2;
+            for (uint32_t q = 0; q < ar.tp; ++q)
+                st_pair2(ar.buf[q] + off, __uint_as_float(*reinterpret_cast<const uint32_t*>(&lo)),
+                         __uint_as_float(*reinterpret_cast<const uint32_t*>(&hi)), flag);
+        }
+        const uint2* mine = ar.buf[ar.rank];
+        const long long t0 = clock64();
+        for (uint32_t g = threadIdx.x; g < g4; g += blockDim.x) {
+            const uint32_t m = (g * 4) / GV_COLS, c = (g * 4) % GV_COLS, n = n0 + c;
+            if (n >= N) continue;
+            float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (uint32_t q = 0; q < ar.tp; ++q) {
+                const uint2* src = mine + ((uint64_t)(par * ar.tp + q) * GV_MMA_N + m) * NW + n / 2;
+                uint4 w = ld_pair2(src);
+                for (uint32_t spin = 0; w.y != flag || w.w != flag; ++spin) {
+                    if ((spin & 31) == 31) {
+                        if (*reinterpret_cast<volatile int*>(&s_fail) || *reinterpret_cast<volatile unsigned int*>(err)) {
+                            s_fail = 1;
+                            return;
+                        }
+                        if (clock64() - t0 > kSpinLimitCycles / 2) {
+                            atomicCAS(err, 0u, 0x302u);
+                            s_fail = 1;
+                            return;
+                        }
+                    }
+                    w = ld_pair2(src);
+                }
+                const float2 p0 = Elem<T>::to_f2(*reinterpret_cast<const T2*>(&w.x));
+                const float2 p1 = Elem<T>::to_f2(*reinterpret_cast<const T2*>(&w.z));
+                a[0] += p0.x;
+                a[1] += p0.y;
+                a[2] += p1.x;
+                a[3] += p1.y;
+            }
+            T* y = Y + (uint64_t)m * N + n;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) y[e] = Elem<T>::from_f(Elem<T>::to_f(y[e]) + a[e]);
+        }
+        return;
+    }
     const uint32_t groups = Mt * GV_COLS / 2;
     for (uint32_t g = threadIdx.x; g < groups; g += blockDim.x) {
         const uint32_t m = (g * 2) / GV_COLS, c = (g * 2) % GV_COLS;

@@ -194,6 +194,9 @@ ncclDataType_t nccl_type(int dtype) { return dtype == EVKCU_BF16 ? ncclBfloat16 
 // measured at tp = 2 (decode ms per step, fused / NCCL): C3 1 x 512 0.235 /
 // 0.322, C4 8 x 2048 1.78 / 2.22, C5 16 x 4096 7.19 / 6.91.
 constexpr uint64_t kFusedArMaxElems = 32768;
+// Above that, up to this size, the partials travel as 16-bit values (the
+// numerics of NCCL's all-reduce of 16-bit partials, half the fp32 bytes).
+constexpr uint64_t kFusedArHalfMaxElems = 131072;
 
 // Wo / W2 product into the residual.  On one GPU acc_c fuses the add; with
 // tensor parallelism the product is a partial sum, summed across ranks first.
@@ -202,10 +205,16 @@ int proj_residual(evkcu_llm* m, const void* a, const void* w, uint32_t rows, uin
     const uint32_t D = m->cfg.d_model;
     const int dt = m->cfg.dtype;
     if (m->cfg.tp_size == 1) return evkcu_matmul(a, w, m->x, 1, rows, K, D, 0, 0, 0, EVKCU_MM_ACC_C, dt, st);
-    if (decode && rows <= 16 && m->ar_ready && (uint64_t)rows * D <= kFusedArMaxElems) {
+    static const int force_half = [] {
+        const char* e = getenv("EVKCU_FUSED_AR_HALF");
+        return e && atoi(e) ? 1 : 0;
+    }();
+    const uint64_t elems = (uint64_t)rows * D;
+    if (decode && rows <= 16 && m->ar_ready && elems <= kFusedArHalfMaxElems) {
         // GEMV + all-reduce over NVLink peer memory + residual add, one kernel.
         GemvAllReduce ar = m->ar;
         ar.callsite = callsite;
+        ar.half = (force_half || elems > kFusedArMaxElems) ? 1u : 0u;
         return gemv_allreduce_residual(a, w, m->x, rows, K, D, ar, dt, st);
     }
     LLM_TRY(evkcu_matmul(a, w, m->tmp, 1, rows, K, D, 0, 0, 0, 0, dt, st));
