@@ -716,6 +716,7 @@ constexpr int GV_COLS = 128;
 constexpr int GV_BK = 64;
 constexpr int GV_MMA_N = 16;
 constexpr int GV_STAGES = 6;
+constexpr int GV_EARLY = 4;  // weight tiles requested before griddepcontrol.wait
 constexpr int GV_W_BYTES = GV_COLS * GV_BK * 2;    // 16 KB
 constexpr int GV_X_BYTES = GV_MMA_N * GV_BK * 2;   // 2 KB
 constexpr int GV_STAGE_BYTES = GV_W_BYTES + GV_X_BYTES;
@@ -796,16 +797,25 @@ __global__ void __launch_bounds__(GV_THREADS, 2)
                     tma_load_3d(w + GV_W_BYTES / 2, &tmW, &full[s], (int)n0 + 64, k0, 0);
                 }
             };
-            // The weights are constant: the first ring of W tiles is requested
-            // before waiting for the kernels that produce x.
+            // The weights are constant: the first GV_EARLY W tiles are
+            // requested before waiting for the kernels that produce x, the
+            // rest of the ring after it, each behind its stage's x tile (x
+            // queued behind a full ring of weight tiles arrives later:
+            // 4 early tiles measured 2-4 % faster than 6 on the C4 GEMVs).
             const uint32_t pre = min(nkt, (uint32_t)GV_STAGES);
-            for (uint32_t i = 0; i < pre; ++i) {
+            const uint32_t early = min(pre, (uint32_t)GV_EARLY);
+            for (uint32_t i = 0; i < early; ++i) {
                 mbar_arrive_expect_tx(&full[i], GV_STAGE_BYTES);
                 load_w(i, (int)i);
             }
             pdl_wait();
-            for (uint32_t i = 0; i < pre; ++i)
+            for (uint32_t i = 0; i < pre; ++i) {
+                if (i >= early) {
+                    mbar_arrive_expect_tx(&full[i], GV_STAGE_BYTES);
+                    load_w(i, (int)i);
+                }
                 tma_load_3d(sX + i * GV_X_BYTES, &tmX, &full[i], (int)((kt0 + i) * GV_BK), 0, 0);
+            }
             for (uint32_t i = pre; i < nkt; ++i) {
                 const int s = i % GV_STAGES;
                 if (!mbar_wait(&empty[s], ((i / GV_STAGES) & 1) ^ 1, s_abort, err, kTimeoutGemv)) break;
