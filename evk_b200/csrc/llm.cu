@@ -210,7 +210,11 @@ int proj_residual(evkcu_llm* m, const void* a, const void* w, uint32_t rows, uin
         return e && atoi(e) ? 1 : 0;
     }();
     const uint64_t elems = (uint64_t)rows * D;
-    if (decode && rows <= 16 && m->ar_ready && elems <= kFusedArHalfMaxElems) {
+    // The 16-bit form is used on its own only at tp = 2, where it was measured
+    // against NCCL; the switch forces it at any tp (the TP test).
+    const bool half_ok = force_half || m->cfg.tp_size == 2;
+    const bool fuse = elems <= kFusedArMaxElems || (half_ok && elems <= kFusedArHalfMaxElems);
+    if (decode && rows <= 16 && m->ar_ready && fuse) {
         // GEMV + all-reduce over NVLink peer memory + residual add, one kernel.
         GemvAllReduce ar = m->ar;
         ar.callsite = callsite;

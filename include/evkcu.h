@@ -350,9 +350,9 @@ uint32_t evkcu_llm_length(const evkcu_llm* m);
 /* 1 when the decode Wo / W2 all-reduce of this tensor-parallel model can run
  * fused over peer memory (every rank mapped its peers and none set
  * EVKCU_DISABLE_FUSED_ALLREDUCE; the ranks agree at creation), 0 when it
- * uses NCCL.  Even when 1, calls of more than 131,072 elements (batch rows x
- * d_model) use NCCL; above 32,768 the fused path sends 16-bit partials.
- * Host value.                                                                */
+ * uses NCCL.  Even when 1, calls of more than 32,768 elements (batch rows x
+ * d_model) use NCCL, except at tp = 2 up to 131,072, where the fused path
+ * sends 16-bit partials.  Host value.                                        */
 uint32_t evkcu_llm_fused_allreduce(const evkcu_llm* m);
 
 #ifdef __cplusplus
